@@ -1,0 +1,380 @@
+// sm_100a software ASTC LDR decoder (device side).
+//
+// B200 has no ASTC texture hardware, so blocks are decoded with integer ALU
+// work in two stages that every kernel in this library shares:
+//
+//   Stage A, one thread per 16-byte block (`decode_header`): block mode,
+//   partition count/seed, colour endpoint modes, BISE colour integers ->
+//   8-bit endpoint pairs per partition, BISE weight integers -> unquantised
+//   0..64 grid weights. Results land in a `BlockDesc` plus a 64-byte weight
+//   array in shared memory.
+//
+//   Stage B, one thread per texel (`texel_c16`): partition from the
+//   precomputed pattern table, weight (direct or bilinear infill), endpoint
+//   interpolation to the 16-bit value C.
+//
+// Views of C (the values the reference's astcenc F32 output carries, see
+// astc_kv/bridge.cpp:27-35): UNORM8 = C >> 8; fp16 = 1.0 for C == 65535,
+// otherwise C/65536 truncated to fp16.
+//
+// Illegal encodings (reserved modes, over-long weight/colour streams, HDR
+// endpoint modes or HDR void-extent in this LDR profile, malformed
+// void-extent) decode to the error colour: magenta (1, 0, 1, 1).
+#pragma once
+#include <cstdint>
+
+#include "akv_tables.h"
+
+namespace akv {
+
+// The decode tables, in static device memory of the (single) translation
+// unit that includes this header; akv_cuda_init fills them per device.
+__device__ Tables g_akv_tables;
+
+// BlockDesc.info layout.
+enum : uint32_t {
+    kInfoParts = 0,     // 2 bits: partition count - 1
+    kInfoVoid = 2,      // 1 bit: void-extent block (ep holds UNORM16 colours)
+    kInfoDual = 3,      // 1 bit
+    kInfoCcs = 4,       // 2 bits: channel on plane 1
+    kInfoReduced = 6,   // 1 bit: weight grid smaller than the footprint
+    kInfoWx = 8,        // 4 bits
+    kInfoWy = 12,       // 4 bits
+    kInfoError = 16,    // 1 bit: decoded as the error colour
+};
+
+// NCH = channels the caller needs (1: R only, as in the scalar layout; 4: RGBA).
+template <int NCH>
+struct BlockDesc {
+    uint32_t pat[2];        // 2-bit partition per texel (texels 0..31; enough for <= 6x6)
+    uint32_t pat_hi[2];     // texels 32..63 (8x8)
+    uint32_t ep[4 * NCH];   // per partition/channel: e0 | e1 << 8, or UNORM16 colour when void
+    uint32_t info;
+};
+
+__device__ __forceinline__ uint32_t bits_u128(uint64_t lo, uint64_t hi, int pos, int n) {
+    // n <= 32, 0 <= pos < 128
+    uint64_t w = pos >= 64 ? (hi >> (pos - 64)) : (pos == 0 ? lo : ((lo >> pos) | (hi << (64 - pos))));
+    return static_cast<uint32_t>(w) & (n >= 32 ? 0xFFFFFFFFu : ((1u << n) - 1u));
+}
+
+__device__ __forceinline__ uint64_t window_u128(uint64_t lo, uint64_t hi, int pos) {
+    // 64 bits starting at pos (bits past 127 read as zero)
+    if (pos == 0) return lo;
+    if (pos >= 64) return pos >= 128 ? 0ull : (hi >> (pos - 64));
+    return (lo >> pos) | (hi << (64 - pos));
+}
+
+// Keep only bits [0, n) of a 128-bit value.
+__device__ __forceinline__ void mask_u128(uint64_t& lo, uint64_t& hi, int n) {
+    if (n <= 0) { lo = hi = 0; return; }
+    if (n < 64) { lo &= (1ull << n) - 1ull; hi = 0; return; }
+    if (n == 64) { hi = 0; return; }
+    if (n < 128) hi &= (1ull << (n - 64)) - 1ull;
+}
+
+// Decode one BISE value group. `win` holds the group's bits at bit 0.
+// Returns the digits of the trit/quint block packed (2 bits per trit, 3 per quint).
+__device__ __forceinline__ uint32_t group_digits(uint64_t win, int b, int trits, int quints) {
+    const Tables& T = g_akv_tables;
+    if (trits) {
+        uint32_t t = static_cast<uint32_t>((win >> b) & 3u) |
+                     static_cast<uint32_t>(((win >> (2 * b + 2)) & 3u) << 2) |
+                     static_cast<uint32_t>(((win >> (3 * b + 4)) & 1u) << 4) |
+                     static_cast<uint32_t>(((win >> (4 * b + 5)) & 3u) << 5) |
+                     static_cast<uint32_t>(((win >> (5 * b + 7)) & 1u) << 7);
+        return __ldg(&T.trit[t]);
+    }
+    if (quints) {
+        uint32_t qv = static_cast<uint32_t>((win >> b) & 7u) |
+                      static_cast<uint32_t>(((win >> (2 * b + 3)) & 3u) << 3) |
+                      static_cast<uint32_t>(((win >> (3 * b + 5)) & 3u) << 5);
+        return __ldg(&T.quint[qv]);
+    }
+    return 0;
+}
+
+// BISE decode of `count` values of range q from the 128-bit stream (lo, hi)
+// that starts at bit 0 and is already masked to its own length.
+// `sink(i, code)` receives each raw code.
+template <typename Sink>
+__device__ __forceinline__ void bise_stream(uint64_t lo, uint64_t hi, int count, int q, Sink&& sink) {
+    const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
+    const int b = shp & 15, trits = (shp >> 4) & 1, quints = (shp >> 5) & 1;
+    const int gs = quints ? 3 : 5;
+    const int gbits = trits ? 5 * b + 8 : (quints ? 3 * b + 7 : 5 * b);
+    const uint32_t mmask = (1u << b) - 1u;
+    int base = 0;
+    for (int i = 0; i < count; i += gs, base += gbits) {
+        const uint64_t win = window_u128(lo, hi, base);
+        const uint32_t dg = group_digits(win, b, trits, quints);
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            if (j >= gs || i + j >= count) break;
+            // Offset of the j-th value's low bits within the group.
+            const int off = j * b + (trits ? (j == 0 ? 0 : j == 1 ? 2 : j == 2 ? 4 : j == 3 ? 5 : 7)
+                                           : (quints ? (j == 0 ? 0 : j == 1 ? 3 : 5) : 0));
+            const uint32_t m = static_cast<uint32_t>(win >> off) & mmask;
+            const uint32_t d = trits ? ((dg >> (2 * j)) & 3u) : (quints ? ((dg >> (3 * j)) & 7u) : 0u);
+            sink(i + j, static_cast<int>((d << b) | m));
+        }
+    }
+}
+
+// Number of bits in a BISE stream (device copy of bise_stream_bits).
+__device__ __forceinline__ int bise_stream_bits_dev(int count, int q) {
+    const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
+    const int b = shp & 15;
+    return count * b + (((shp >> 4) & 1) ? (8 * count + 4) / 5 : 0) + (((shp >> 5) & 1) ? (7 * count + 2) / 3 : 0);
+}
+
+__device__ __forceinline__ int clamp8(int v) { return v < 0 ? 0 : (v > 255 ? 255 : v); }
+
+// Signed bit transfer between a (offset) and b (base), spec form.
+__device__ __forceinline__ void bit_xfer(int& a, int& b) {
+    b = (b >> 1) | (a & 0x80);
+    a = (a >> 1) & 0x3F;
+    if (a & 0x20) a -= 0x40;
+}
+
+// LDR endpoint modes -> 8-bit endpoint pair per channel. Returns false for HDR
+// modes (2, 3, 7, 11, 14, 15).
+__device__ __forceinline__ bool endpoints(int cem, const int* v, int e0[4], int e1[4]) {
+    switch (cem) {
+        case 0:
+            e0[0] = e0[1] = e0[2] = v[0]; e1[0] = e1[1] = e1[2] = v[1]; e0[3] = e1[3] = 255;
+            return true;
+        case 1: {
+            const int l0 = (v[0] >> 2) | (v[1] & 0xC0);
+            const int l1 = min(l0 + (v[1] & 0x3F), 255);
+            e0[0] = e0[1] = e0[2] = l0; e1[0] = e1[1] = e1[2] = l1; e0[3] = e1[3] = 255;
+            return true;
+        }
+        case 4:
+            e0[0] = e0[1] = e0[2] = v[0]; e1[0] = e1[1] = e1[2] = v[1]; e0[3] = v[2]; e1[3] = v[3];
+            return true;
+        case 5: {
+            int a0 = v[1], b0 = v[0], a1 = v[3], b1 = v[2];
+            bit_xfer(a0, b0);
+            bit_xfer(a1, b1);
+            e0[0] = e0[1] = e0[2] = b0; e0[3] = b1;
+            e1[0] = e1[1] = e1[2] = clamp8(b0 + a0); e1[3] = clamp8(b1 + a1);
+            return true;
+        }
+        case 6:
+        case 10:
+            for (int c = 0; c < 3; ++c) { e0[c] = (v[c] * v[3]) >> 8; e1[c] = v[c]; }
+            e0[3] = cem == 10 ? v[4] : 255;
+            e1[3] = cem == 10 ? v[5] : 255;
+            return true;
+        case 8:
+        case 12: {
+            const int a0 = cem == 12 ? v[6] : 255, a1 = cem == 12 ? v[7] : 255;
+            if (v[1] + v[3] + v[5] >= v[0] + v[2] + v[4]) {
+                e0[0] = v[0]; e0[1] = v[2]; e0[2] = v[4]; e0[3] = a0;
+                e1[0] = v[1]; e1[1] = v[3]; e1[2] = v[5]; e1[3] = a1;
+            } else {  // blue contraction, endpoints swapped
+                e0[0] = (v[1] + v[5]) >> 1; e0[1] = (v[3] + v[5]) >> 1; e0[2] = v[5]; e0[3] = a1;
+                e1[0] = (v[0] + v[4]) >> 1; e1[1] = (v[2] + v[4]) >> 1; e1[2] = v[4]; e1[3] = a0;
+            }
+            return true;
+        }
+        case 9:
+        case 13: {
+            int o[4], bse[4];
+            for (int c = 0; c < 3; ++c) { o[c] = v[2 * c + 1]; bse[c] = v[2 * c]; bit_xfer(o[c], bse[c]); }
+            if (cem == 13) { o[3] = v[7]; bse[3] = v[6]; bit_xfer(o[3], bse[3]); }
+            else { o[3] = 0; bse[3] = 255; }
+            int lo[4], hi[4];
+            for (int c = 0; c < 4; ++c) { lo[c] = bse[c]; hi[c] = bse[c] + o[c]; }
+            if (o[0] + o[1] + o[2] < 0) {  // blue contraction, endpoints swapped
+                int t[4];
+                for (int c = 0; c < 4; ++c) { t[c] = hi[c]; hi[c] = lo[c]; lo[c] = t[c]; }
+                lo[0] = (lo[0] + lo[2]) >> 1; lo[1] = (lo[1] + lo[2]) >> 1;
+                hi[0] = (hi[0] + hi[2]) >> 1; hi[1] = (hi[1] + hi[2]) >> 1;
+            }
+            for (int c = 0; c < 4; ++c) { e0[c] = clamp8(lo[c]); e1[c] = clamp8(hi[c]); }
+            return true;
+        }
+        default:
+            return false;
+    }
+}
+
+// Stage A. `blk` is the raw 16-byte block; `fp` the footprint index (0/1/2 for
+// 4x4/6x6/8x8). Writes `d` and the unquantised grid weights `w` (plane
+// interleaved, up to 64 entries).
+template <int NCH>
+__device__ __forceinline__ void decode_header(uint4 blk, int fp, BlockDesc<NCH>& d, uint8_t* w) {
+    const Tables& T = g_akv_tables;
+    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
+    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
+    const int mode = static_cast<int>(lo & 0x7FF);
+
+    auto set_error = [&]() {
+        d.info = (1u << kInfoError);
+        d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) d.ep[c] = (c == 1) ? 0u : 0xFFFFu;  // e0 = e1 = 255 or 0
+        w[0] = 0;
+    };
+
+    if ((mode & 0x1FF) == 0x1FC) {
+        // Void extent: bit 9 = HDR (error here), bits 10..11 reserved = 1,
+        // four 13-bit extent coordinates, then RGBA UNORM16 at bits 64..127.
+        const uint32_t s0 = bits_u128(lo, hi, 12, 13), s1 = bits_u128(lo, hi, 25, 13);
+        const uint32_t t0 = bits_u128(lo, hi, 38, 13), t1 = bits_u128(lo, hi, 51, 13);
+        const bool all_ones = (s0 & s1 & t0 & t1) == 0x1FFF;
+        if ((mode & 0x200) || ((lo >> 10) & 3) != 3 || (!all_ones && (s0 >= s1 || t0 >= t1))) { set_error(); return; }
+        d.info = (1u << kInfoVoid);
+        d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) d.ep[c] = static_cast<uint32_t>((hi >> (16 * c)) & 0xFFFF);
+        w[0] = 0;
+        return;
+    }
+
+    const uint32_t me = __ldg(&T.mode[fp][mode]);
+    if (!(me & kModeValid)) { set_error(); return; }
+    const int dual = (me & kModeDual) ? 1 : 0;
+    const int wq = mode_wq(me), wx = mode_wx(me), wy = mode_wy(me), wbits = mode_wbits(me);
+    const int parts = static_cast<int>((lo >> 11) & 3) + 1;
+    if (dual && parts == 4) { set_error(); return; }
+
+    const int top = 128 - wbits - 2 * dual;  // first bit above the colour data
+    int cem[4];
+    int cstart, extra = 0, seed = 0;
+    if (parts == 1) {
+        cem[0] = static_cast<int>((lo >> 13) & 15);
+        cstart = 17;
+    } else {
+        seed = static_cast<int>((lo >> 13) & 0x3FF);
+        const int field = static_cast<int>((lo >> 23) & 0x3F);
+        cstart = 29;
+        if ((field & 3) == 0) {
+            for (int p = 0; p < 4; ++p) cem[p] = field >> 2;
+        } else {
+            extra = 3 * parts - 4;
+            const int all = (field >> 2) | (static_cast<int>(bits_u128(lo, hi, top - extra, extra)) << 4);
+            const int cls = (field & 3) - 1;
+            for (int p = 0; p < 4; ++p)
+                cem[p] = ((cls + ((all >> p) & 1)) << 2) | ((all >> (parts + 2 * p)) & 3);
+        }
+    }
+    int npairs = 0;
+    for (int p = 0; p < parts; ++p) npairs += (cem[p] >> 2) + 1;
+    const int avail = top - extra - cstart;
+    if (npairs > 9 || avail < 0) { set_error(); return; }
+    const int cq = T.cquant[npairs][avail];
+    if (cq == 0xFF) { set_error(); return; }
+
+    // Colour integers.
+    int vals[18];
+    {
+        uint64_t clo = window_u128(lo, hi, cstart);
+        uint64_t chi = cstart == 0 ? hi : (hi >> cstart);
+        const int cbits = bise_stream_bits_dev(2 * npairs, cq);
+        mask_u128(clo, chi, cbits);
+        bise_stream(clo, chi, 2 * npairs, cq, [&](int i, int code) { vals[i] = __ldg(&T.cunq[cq][code]); });
+    }
+    int e0[4][4], e1[4][4];
+    {
+        int k = 0;
+        for (int p = 0; p < parts; ++p) {
+            if (!endpoints(cem[p], vals + k, e0[p], e1[p])) { set_error(); return; }
+            k += 2 * ((cem[p] >> 2) + 1);
+        }
+    }
+
+    // Weights: the stream runs downward from bit 127; bit-reverse the block.
+    {
+        uint64_t wlo = __brevll(hi), whi = __brevll(lo);
+        mask_u128(wlo, whi, wbits);
+        const int n = wx * wy * (dual + 1);
+        bise_stream(wlo, whi, n, wq, [&](int i, int code) { w[i] = __ldg(&T.wunq[wq][code]); });
+    }
+
+    const int ccs = dual ? static_cast<int>(bits_u128(lo, hi, 128 - wbits - 2, 2)) : 0;
+    d.info = static_cast<uint32_t>(parts - 1) | (dual << kInfoDual) | (ccs << kInfoCcs) |
+             ((me & kModeReduced) ? (1u << kInfoReduced) : 0u) | (wx << kInfoWx) | (wy << kInfoWy);
+    if (parts > 1) {
+        const uint32_t* pt = T.part[fp][parts - 2][seed];
+        d.pat[0] = __ldg(pt + 0); d.pat[1] = __ldg(pt + 1);
+        d.pat_hi[0] = __ldg(pt + 2); d.pat_hi[1] = __ldg(pt + 3);
+    } else {
+        d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0;
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+            d.ep[p * NCH + c] = (p < parts) ? static_cast<uint32_t>(e0[p][c] | (e1[p][c] << 8)) : 0u;
+}
+
+
+// Stage B: 16-bit values C of texel (x, y) for the NCH channels the
+// descriptor holds (channel c of the descriptor is RGBA channel c).
+template <int BS, int NCH>
+__device__ __forceinline__ void texel_values(const BlockDesc<NCH>& d, const uint8_t* w, int x, int y, uint32_t* out) {
+    const uint32_t info = d.info;
+    if (info & (1u << kInfoVoid)) {
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) out[c] = d.ep[c];
+        return;
+    }
+    const int t = y * BS + x;
+    int part = 0;
+    if (info & 3u) {
+        const uint32_t word = t < 16 ? d.pat[0] : t < 32 ? d.pat[1] : t < 48 ? d.pat_hi[0] : d.pat_hi[1];
+        part = (word >> (2 * (t & 15))) & 3;
+    }
+    const int dual = (info >> kInfoDual) & 1;
+    const int ccs = (info >> kInfoCcs) & 3;
+    int wt0 = 0, wt1 = 0;
+    if (info & (1u << kInfoError)) {
+        wt0 = wt1 = 0;
+    } else if (!(info & (1u << kInfoReduced))) {
+        wt0 = w[t << dual];
+        wt1 = dual ? w[(t << 1) + 1] : wt0;
+    } else {
+        const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
+        constexpr int kDs = (1024 + BS / 2) / (BS - 1);
+        const int gs = (kDs * x * (wx - 1) + 32) >> 6;
+        const int gt = (kDs * y * (wy - 1) + 32) >> 6;
+        const int js = gs >> 4, fs = gs & 15, jt = gt >> 4, ft = gt & 15;
+        const int w11 = (fs * ft + 8) >> 4;
+        const int f00 = 16 - fs - ft + w11, f01 = fs - w11, f10 = ft - w11;
+        const int i00 = js + jt * wx;
+        const bool has_x = js + 1 < wx, has_y = jt + 1 < wy;
+#pragma unroll
+        for (int pl = 0; pl < 2; ++pl) {
+            if (pl == 1 && !dual) { wt1 = wt0; break; }
+            const int p00 = w[(i00 << dual) + pl];
+            const int p01 = has_x ? w[((i00 + 1) << dual) + pl] : 0;
+            const int p10 = has_y ? w[((i00 + wx) << dual) + pl] : 0;
+            const int p11 = (has_x && has_y) ? w[((i00 + wx + 1) << dual) + pl] : 0;
+            const int v = (p00 * f00 + p01 * f01 + p10 * f10 + p11 * w11 + 8) >> 4;
+            if (pl == 0) wt0 = v; else wt1 = v;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+        const int wt = (dual && ccs == c) ? wt1 : wt0;
+        const uint32_t ep = d.ep[part * NCH + c];
+        const int e0 = ep & 0xFF, e1 = (ep >> 8) & 0xFF;
+        // C = ((e0*257)*(64-w) + (e1*257)*w + 32) >> 6 = 4X + ((X + 32) >> 6),
+        // with X = e0*(64-w) + e1*w.
+        const int X = e0 * (64 - wt) + e1 * wt;
+        out[c] = static_cast<uint32_t>(4 * X + ((X + 32) >> 6));
+    }
+}
+
+// fp16 view of C as float (exact): 1.0 for 65535, else C/65536 truncated to 11
+// significant bits.
+__device__ __forceinline__ float c16_to_unit(uint32_t c) {
+    const float f = __int_as_float(__float_as_int(static_cast<float>(c)) & 0xFFFFE000) * 0x1p-16f;
+    return c == 0xFFFFu ? 1.0f : f;
+}
+
+
+}  // namespace akv

@@ -1,0 +1,360 @@
+// C-ABI entry points of libakv_cuda.so (declared in include/akv_cuda.h).
+//
+// Host side: argument validation, per-device table set-up, launch-shape
+// choice and template dispatch. Device side: the kernels in
+// akv_decode_kernels.cuh and akv_attention_kernels.cuh.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/akv_cuda.h"
+#include "akv_attention_kernels.cuh"
+#include "akv_decode_kernels.cuh"
+#include "akv_tables.h"
+
+namespace akv {
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_init_mu;
+bool g_init_done[kMaxDevices];
+Tables* g_host_tables = nullptr;
+
+const Tables& host_tables() {
+    static std::once_flag once;
+    std::call_once(once, [] {
+        g_host_tables = new Tables;
+        build_tables(g_host_tables);
+    });
+    return *g_host_tables;
+}
+
+int init_device(int device) {
+    if (device < 0 || device >= kMaxDevices) return AKV_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> lock(g_init_mu);
+    if (g_init_done[device]) return AKV_OK;
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return AKV_ERR_CUDA;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return AKV_ERR_CUDA;
+    const Tables& t = host_tables();
+    cudaError_t e = cudaMemcpyToSymbol(g_akv_tables, &t, sizeof(Tables), 0, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return AKV_ERR_CUDA;
+    g_init_done[device] = true;
+    return AKV_OK;
+}
+
+int ensure_init() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return AKV_ERR_CUDA;
+    if (dev >= 0 && dev < kMaxDevices && g_init_done[dev]) return AKV_OK;
+    // Table upload is synchronous; refuse inside a stream capture.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(cudaStreamLegacy, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
+        return AKV_ERR_NOT_INITIALIZED;
+    return init_device(dev);
+}
+
+int sm_count() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+inline int launch_status() {
+    return cudaPeekAtLastError() == cudaSuccess ? AKV_OK : (cudaGetLastError(), AKV_ERR_CUDA);
+}
+
+bool valid_block(int b) { return b == 4 || b == 6 || b == 8; }
+
+// ---------------------------------------------------------------- attention
+
+template <int D, int G, int KBS, int VBS, int VL>
+int launch_attention(const AttnParams& p, cudaStream_t s) {
+    using Cfg = AttnCfg<D, G, KBS, VBS, VL>;
+    static_assert(Cfg::TG * G <= 2 * Cfg::CH || KBS == 0, "reduction fits");
+    static_assert(Cfg::TG * G <= Cfg::CH, "reduction fits in the V tile");
+    auto kern = attn_split_kernel<D, G, KBS, VBS, VL>;
+    const size_t smem = Cfg::kSmem;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return AKV_ERR_CUDA;
+    }
+    dim3 grid(p.nsplits, p.Hkv, p.B);
+    kern<<<grid, kAttnThreads, smem, s>>>(p);
+    int st = launch_status();
+    if (st) return st;
+    merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+    return launch_status();
+}
+
+int chunk_tokens(int kbs, int vbs) { return vbs ? 8 * vbs : (kbs ? 8 * kbs : 64); }
+
+using Launcher = int (*)(const AttnParams&, cudaStream_t);
+
+struct Variant {
+    int D, G, kbs, vbs, vl;
+    Launcher fn;
+};
+
+// Compiled (head_dim, group, K footprint (0 = fp16), V footprint (0 = fp16),
+// V layout) combinations: the reference fixtures' shapes and the five
+// benchmark configurations.
+#define AKV_VARIANT(D, G, KB, VB, VL) {D, G, KB, VB, VL, &launch_attention<D, G, KB, VB, VL>}
+const Variant kVariants[] = {
+    AKV_VARIANT(64, 3, 0, 4, AKV_LAYOUT_RGBA),     // SmolLM2 shape, rgba 4x4 V (configs 0/1)
+    AKV_VARIANT(64, 3, 0, 4, AKV_LAYOUT_SCALAR),
+    AKV_VARIANT(64, 3, 0, 6, AKV_LAYOUT_SCALAR),   // reference fixtures, scalar 6x6 V
+    AKV_VARIANT(64, 3, 6, 6, AKV_LAYOUT_SCALAR),   // reference fixtures, 6x6 K and V
+    AKV_VARIANT(64, 3, 0, 8, AKV_LAYOUT_SCALAR),
+    AKV_VARIANT(64, 3, 0, 0, AKV_LAYOUT_SCALAR),   // FP16 control
+    AKV_VARIANT(128, 4, 0, 6, AKV_LAYOUT_SCALAR),  // Llama-3-8B shape, 6x6 V (config 2)
+    AKV_VARIANT(128, 4, 0, 4, AKV_LAYOUT_SCALAR),  // ragged paged atlas, 4x4 V (config 4)
+    AKV_VARIANT(128, 4, 0, 8, AKV_LAYOUT_SCALAR),
+    AKV_VARIANT(128, 4, 0, 4, AKV_LAYOUT_RGBA),
+    AKV_VARIANT(128, 4, 0, 0, AKV_LAYOUT_SCALAR),  // FP16 control
+    AKV_VARIANT(128, 8, 4, 8, AKV_LAYOUT_SCALAR),  // Llama-3-70B shape, 4x4 K + 8x8 V (config 3)
+    AKV_VARIANT(128, 8, 0, 8, AKV_LAYOUT_SCALAR),
+    AKV_VARIANT(128, 8, 0, 0, AKV_LAYOUT_SCALAR),  // FP16 control
+};
+#undef AKV_VARIANT
+
+const Variant* find_variant(int D, int G, int kbs, int vbs, int vl) {
+    for (const Variant& v : kVariants)
+        if (v.D == D && v.G == G && v.kbs == kbs && v.vbs == vbs && (vbs == 0 || v.vl == vl)) return &v;
+    return nullptr;
+}
+
+struct AttnPlan {
+    int kbs, vbs, vl, split, nsplits;
+    size_t ws;
+};
+
+int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
+    if (!d) return AKV_ERR_INVALID_ARGUMENT;
+    if (d->batch <= 0 || d->q_heads <= 0 || d->kv_heads <= 0 || d->head_dim <= 0 || d->max_tokens <= 0 ||
+        d->page_tokens <= 0 || d->q_heads % d->kv_heads)
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (d->q_dtype < AKV_Q_F32 || d->q_dtype > AKV_Q_F16) return AKV_ERR_INVALID_ARGUMENT;
+    const AkvPlane* planes[2] = {&d->k, &d->v};
+    int fps[2] = {0, 0};
+    for (int i = 0; i < 2; ++i) {
+        const AkvPlane* pl = planes[i];
+        if (!pl->data) return AKV_ERR_INVALID_ARGUMENT;
+        if (pl->storage == AKV_STORAGE_ASTC) {
+            if (!valid_block(pl->block) || d->page_tokens % pl->block) return AKV_ERR_INVALID_ARGUMENT;
+            if (pl->layout != AKV_LAYOUT_SCALAR && pl->layout != AKV_LAYOUT_RGBA) return AKV_ERR_INVALID_ARGUMENT;
+            if (pl->layout == AKV_LAYOUT_RGBA && d->head_dim % 4) return AKV_ERR_INVALID_ARGUMENT;
+            if (pl->normalization < AKV_NORM_PAGE_CHANNEL || pl->normalization > AKV_NORM_BLOCK_AFFINE)
+                return AKV_ERR_INVALID_ARGUMENT;
+            if (!pl->offsets || !pl->scales) return AKV_ERR_INVALID_ARGUMENT;
+            if (i == 0 && pl->layout != AKV_LAYOUT_SCALAR) return AKV_ERR_UNSUPPORTED;
+            if (reinterpret_cast<uintptr_t>(pl->data) % 16) return AKV_ERR_INVALID_ARGUMENT;
+            fps[i] = pl->block;
+        } else if (pl->storage == AKV_STORAGE_FP16) {
+            if (reinterpret_cast<uintptr_t>(pl->data) % 16 || (d->head_dim * 2) % 16) return AKV_ERR_INVALID_ARGUMENT;
+        } else {
+            return AKV_ERR_INVALID_ARGUMENT;
+        }
+        if (pl->side && (i != 0 || pl->storage != AKV_STORAGE_ASTC || pl->side_count <= 0 || !pl->side_channels_dev))
+            return AKV_ERR_INVALID_ARGUMENT;
+    }
+    if (d->block_table_dev && (d->pages_per_seq <= 0 || d->num_pages <= 0 ||
+                               static_cast<int64_t>(d->pages_per_seq) * d->page_tokens < d->max_tokens))
+        return AKV_ERR_INVALID_ARGUMENT;
+    out->kbs = fps[0];
+    out->vbs = fps[1];
+    out->vl = d->v.storage == AKV_STORAGE_ASTC ? d->v.layout : AKV_LAYOUT_SCALAR;
+    if (!find_variant(d->head_dim, d->q_heads / d->kv_heads, out->kbs, out->vbs, out->vl)) return AKV_ERR_UNSUPPORTED;
+    const int ch = chunk_tokens(out->kbs, out->vbs);
+    int split = d->split_tokens;
+    if (split <= 0) {
+        // Enough (split, head, batch) units for ~8 CTAs per SM.
+        const int64_t units = static_cast<int64_t>(d->batch) * d->kv_heads;
+        const int64_t want = (static_cast<int64_t>(sm_count()) * 8 + units - 1) / units;
+        int64_t per = (d->max_tokens + want - 1) / want;
+        per = ((per + ch - 1) / ch) * ch;
+        split = static_cast<int>(per < ch ? ch : per);
+    }
+    int lcm_fp = out->kbs ? out->kbs : 1;
+    if (out->vbs) {
+        int a = lcm_fp, b = out->vbs;
+        while (b) { const int r = a % b; a = b; b = r; }
+        lcm_fp = lcm_fp / a * out->vbs;
+    }
+    if (split % lcm_fp) return AKV_ERR_INVALID_ARGUMENT;
+    out->split = split;
+    out->nsplits = (d->max_tokens + split - 1) / split;
+    out->ws = static_cast<size_t>(d->batch) * d->q_heads * out->nsplits * (d->head_dim + 2) * sizeof(float);
+    return AKV_OK;
+}
+
+// ------------------------------------------------------------------ decode
+
+template <int BS>
+int launch_decode(const void* blocks, int64_t n, int mode, void* out, cudaStream_t s) {
+    const int64_t iters = (n + kDecodeBlocksPerIter - 1) / kDecodeBlocksPerIter;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    const int grid = static_cast<int>(iters < cap ? iters : cap);
+    const uint4* b = static_cast<const uint4*>(blocks);
+    if (mode == AKV_OUT_UNORM8) decode_blocks_kernel<BS, AKV_OUT_UNORM8><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    else if (mode == AKV_OUT_FP16) decode_blocks_kernel<BS, AKV_OUT_FP16><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    else decode_blocks_kernel<BS, AKV_OUT_UNORM16><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    return launch_status();
+}
+
+template <int BS, int LAYOUT>
+int launch_restore(const PlaneDev& pl, int B, int H, int T, int D, int P, const int32_t* table, int pps, int num_pages,
+                   float* out, int32_t* status, cudaStream_t s) {
+    constexpr int CH = 8 * BS;
+    const size_t smem = sizeof(TileScratch<BS, LAYOUT>) + static_cast<size_t>(CH) * D * sizeof(float);
+    auto kern = restore_plane_kernel<BS, LAYOUT>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return AKV_ERR_CUDA;
+    }
+    dim3 grid((T + CH - 1) / CH, H, B);
+    kern<<<grid, kDecodeThreads, smem, s>>>(pl, D, T, P, table, pps, num_pages, out, status);
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace akv
+
+using namespace akv;
+
+extern "C" {
+
+const char* akv_cuda_error(int code) {
+    switch (code) {
+        case AKV_OK: return "success";
+        case AKV_ERR_INVALID_ARGUMENT: return "invalid argument (pointer, size, alignment or shape)";
+        case AKV_ERR_UNSUPPORTED: return "unsupported combination of head_dim, GQA group, footprints and layout";
+        case AKV_ERR_CUDA: return "CUDA runtime error";
+        case AKV_ERR_NOT_INITIALIZED: return "decode tables not initialised on this device (call akv_cuda_init outside stream capture)";
+        case AKV_ERR_BAD_BLOCK_TABLE: return "block table entry outside [0, num_pages)";
+        case AKV_ERR_WORKSPACE: return "workspace missing or smaller than akv_cuda_attention_workspace()";
+        default: return "unknown status code";
+    }
+}
+
+int akv_cuda_abi_version(void) { return AKV_CUDA_ABI_VERSION; }
+
+int akv_cuda_init(int device) { return init_device(device); }
+
+size_t akv_cuda_struct_size(int which) {
+    return which == 0 ? sizeof(AkvPlane) : which == 1 ? sizeof(AkvAttnDesc) : 0;
+}
+
+size_t akv_cuda_host_tables(void* out, size_t bytes) {
+    const Tables& t = host_tables();
+    if (out && bytes >= sizeof(Tables)) std::memcpy(out, &t, sizeof(Tables));
+    return sizeof(Tables);
+}
+
+int akv_cuda_decode_blocks(const void* blocks_dev, int64_t nblocks, int block, int out_mode, void* out_dev, void* stream) {
+    if (nblocks < 0 || !valid_block(block) || out_mode < AKV_OUT_UNORM8 || out_mode > AKV_OUT_UNORM16)
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (nblocks == 0) return AKV_OK;
+    if (!blocks_dev || !out_dev || reinterpret_cast<uintptr_t>(blocks_dev) % 16 ||
+        reinterpret_cast<uintptr_t>(out_dev) % (out_mode == AKV_OUT_UNORM8 ? 4 : 8))
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (int st = ensure_init()) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (block) {
+        case 4: return launch_decode<4>(blocks_dev, nblocks, out_mode, out_dev, s);
+        case 6: return launch_decode<6>(blocks_dev, nblocks, out_mode, out_dev, s);
+        default: return launch_decode<8>(blocks_dev, nblocks, out_mode, out_dev, s);
+    }
+}
+
+int akv_cuda_decode_image(const void* blocks_dev, size_t bytes, int block, float* rgba_dev, unsigned width,
+                          unsigned height, void* stream) {
+    if (!valid_block(block) || width == 0 || height == 0 || width > (1u << 24) || height > (1u << 24))
+        return AKV_ERR_INVALID_ARGUMENT;
+    const int cols = static_cast<int>((width + block - 1) / block), rows = static_cast<int>((height + block - 1) / block);
+    if (static_cast<size_t>(cols) * rows * 16 != bytes) return AKV_ERR_INVALID_ARGUMENT;
+    if (!blocks_dev || !rgba_dev || reinterpret_cast<uintptr_t>(blocks_dev) % 16 || reinterpret_cast<uintptr_t>(rgba_dev) % 16)
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (int st = ensure_init()) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t n = static_cast<int64_t>(cols) * rows;
+    const int64_t iters = (n + kDecodeBlocksPerIter - 1) / kDecodeBlocksPerIter;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+    const int grid = static_cast<int>(iters < cap ? iters : cap);
+    const uint4* b = static_cast<const uint4*>(blocks_dev);
+    const int w = static_cast<int>(width), h = static_cast<int>(height);
+    if (block == 4) decode_image_kernel<4><<<grid, kDecodeThreads, 0, s>>>(b, cols, rows, rgba_dev, w, h);
+    else if (block == 6) decode_image_kernel<6><<<grid, kDecodeThreads, 0, s>>>(b, cols, rows, rgba_dev, w, h);
+    else decode_image_kernel<8><<<grid, kDecodeThreads, 0, s>>>(b, cols, rows, rgba_dev, w, h);
+    return launch_status();
+}
+
+size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc) {
+    AttnPlan plan;
+    return plan_attention(desc, &plan) == AKV_OK ? plan.ws : 0;
+}
+
+int akv_cuda_decode_attention(const AkvAttnDesc* d, void* stream) {
+    AttnPlan plan;
+    if (int st = plan_attention(d, &plan)) return st;
+    if (!d->q_dev || !d->out_dev) return AKV_ERR_INVALID_ARGUMENT;
+    if (!d->workspace_dev || d->workspace_bytes < plan.ws) return AKV_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(d->workspace_dev) % 16) return AKV_ERR_INVALID_ARGUMENT;
+    if (int st = ensure_init()) return st;
+    AttnParams p;
+    p.B = d->batch; p.Hq = d->q_heads; p.Hkv = d->kv_heads; p.T = d->max_tokens;
+    p.page_tokens = d->page_tokens; p.split_tokens = plan.split; p.nsplits = plan.nsplits;
+    p.q_dtype = d->q_dtype; p.q = d->q_dev;
+    p.seq_lens = d->seq_lens_dev; p.table = d->block_table_dev;
+    p.pps = d->pages_per_seq; p.num_pages = d->num_pages;
+    p.k = to_dev(d->k); p.v = to_dev(d->v);
+    const float scale = d->scale > 0.f ? d->scale : 1.0f / std::sqrt(static_cast<float>(d->head_dim));
+    p.qscale = scale * 1.4426950408889634f;
+    float* ws = static_cast<float*>(d->workspace_dev);
+    p.part_acc = ws;
+    p.part_ml = ws + static_cast<size_t>(d->batch) * d->q_heads * plan.nsplits * d->head_dim;
+    p.out = d->out_dev;
+    p.status = d->status_dev;
+    const Variant* v = find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl);
+    return v->fn(p, static_cast<cudaStream_t>(stream));
+}
+
+int akv_cuda_restore_plane(const AkvPlane* plane, int32_t batch, int32_t kv_heads, int32_t max_tokens, int32_t head_dim,
+                           int32_t page_tokens, const int32_t* block_table_dev, int32_t pages_per_seq, int32_t num_pages,
+                           float* out_dev, int32_t* status_dev, void* stream) {
+    if (!plane || !plane->data || !out_dev || batch <= 0 || kv_heads <= 0 || max_tokens <= 0 || head_dim <= 0 ||
+        page_tokens <= 0)
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (block_table_dev && (pages_per_seq <= 0 || num_pages <= 0 ||
+                            static_cast<int64_t>(pages_per_seq) * page_tokens < max_tokens))
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (int st = ensure_init()) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const PlaneDev pl = to_dev(*plane);
+    if (plane->storage == AKV_STORAGE_FP16) {
+        restore_fp16_kernel<<<dim3(max_tokens, kv_heads, batch), 128, 0, s>>>(pl, head_dim, max_tokens, page_tokens,
+                                                                              block_table_dev, pages_per_seq, num_pages,
+                                                                              out_dev, status_dev);
+        return launch_status();
+    }
+    if (plane->storage != AKV_STORAGE_ASTC || !valid_block(plane->block) || page_tokens % plane->block ||
+        !plane->offsets || !plane->scales || reinterpret_cast<uintptr_t>(plane->data) % 16)
+        return AKV_ERR_INVALID_ARGUMENT;
+    if (plane->layout == AKV_LAYOUT_RGBA && head_dim % 4) return AKV_ERR_INVALID_ARGUMENT;
+    const bool rgba = plane->layout == AKV_LAYOUT_RGBA;
+#define AKV_RESTORE(BS, L) launch_restore<BS, L>(pl, batch, kv_heads, max_tokens, head_dim, page_tokens, block_table_dev, \
+                                                  pages_per_seq, num_pages, out_dev, status_dev, s)
+    switch (plane->block) {
+        case 4: return rgba ? AKV_RESTORE(4, AKV_LAYOUT_RGBA) : AKV_RESTORE(4, AKV_LAYOUT_SCALAR);
+        case 6: return rgba ? AKV_RESTORE(6, AKV_LAYOUT_RGBA) : AKV_RESTORE(6, AKV_LAYOUT_SCALAR);
+        default: return rgba ? AKV_RESTORE(8, AKV_LAYOUT_RGBA) : AKV_RESTORE(8, AKV_LAYOUT_SCALAR);
+    }
+#undef AKV_RESTORE
+}
+
+}  // extern "C"

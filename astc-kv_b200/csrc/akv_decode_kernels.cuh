@@ -1,0 +1,113 @@
+// Standalone decode kernels: blocks -> texels, image decode (akv_decode
+// contract), and whole-plane restore to fp32.
+#pragma once
+#include "akv_common.cuh"
+
+namespace akv {
+
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeBlocksPerIter = 128;
+
+// Persistent grid-stride decode of consecutive blocks into
+// out[block][y][x][rgba]. Stage A decodes 128 headers into shared memory,
+// stage B evaluates every texel with consecutive threads on consecutive
+// texels so the output stores coalesce.
+template <int BS, int MODE>
+__global__ void __launch_bounds__(kDecodeThreads) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
+                                                                       void* __restrict__ out) {
+    __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
+    __shared__ uint8_t wts[kDecodeBlocksPerIter][64];
+    constexpr int fp = footprint_index(BS);
+    constexpr int TPB = BS * BS;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kDecodeBlocksPerIter; base < n;
+         base += static_cast<int64_t>(gridDim.x) * kDecodeBlocksPerIter) {
+        const int nb = static_cast<int>(min(static_cast<int64_t>(kDecodeBlocksPerIter), n - base));
+        if (threadIdx.x < nb) decode_header<4>(__ldg(blocks + base + threadIdx.x), fp, desc[threadIdx.x], wts[threadIdx.x]);
+        __syncthreads();
+        const int ntex = nb * TPB;
+        for (int i = threadIdx.x; i < ntex; i += blockDim.x) {
+            const int bi = i / TPB, t = i % TPB;
+            uint32_t c[4];
+            texel_values<BS, 4>(desc[bi], wts[bi], t % BS, t / BS, c);
+            const int64_t o = base * TPB + i;
+            if (MODE == AKV_OUT_UNORM8) {
+                reinterpret_cast<uint32_t*>(out)[o] = (c[0] >> 8) | ((c[1] >> 8) << 8) | ((c[2] >> 8) << 16) | ((c[3] >> 8) << 24);
+            } else if (MODE == AKV_OUT_FP16) {
+                uint2 h;
+                h.x = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[0])))) |
+                      (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[1])))) << 16);
+                h.y = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[2])))) |
+                      (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[3])))) << 16);
+                reinterpret_cast<uint2*>(out)[o] = h;
+            } else {
+                reinterpret_cast<uint2*>(out)[o] = make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// Image decode: float32 RGBA [h][w][4] (fp16 view of C), blocks row-major.
+template <int BS>
+__global__ void __launch_bounds__(kDecodeThreads) decode_image_kernel(const uint4* __restrict__ blocks, int cols, int rows,
+                                                                      float* __restrict__ rgba, int w, int h) {
+    __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
+    __shared__ uint8_t wts[kDecodeBlocksPerIter][64];
+    constexpr int fp = footprint_index(BS);
+    constexpr int TPB = BS * BS;
+    const int64_t n = static_cast<int64_t>(cols) * rows;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * kDecodeBlocksPerIter; base < n;
+         base += static_cast<int64_t>(gridDim.x) * kDecodeBlocksPerIter) {
+        const int nb = static_cast<int>(min(static_cast<int64_t>(kDecodeBlocksPerIter), n - base));
+        if (threadIdx.x < nb) decode_header<4>(__ldg(blocks + base + threadIdx.x), fp, desc[threadIdx.x], wts[threadIdx.x]);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nb * TPB; i += blockDim.x) {
+            const int bi = i / TPB, t = i % TPB;
+            const int64_t blk = base + bi;
+            const int px = static_cast<int>(blk % cols) * BS + t % BS;
+            const int py = static_cast<int>(blk / cols) * BS + t / BS;
+            if (px >= w || py >= h) continue;
+            uint32_t c[4];
+            texel_values<BS, 4>(desc[bi], wts[bi], t % BS, t / BS, c);
+            reinterpret_cast<float4*>(rgba)[static_cast<int64_t>(py) * w + px] =
+                make_float4(c16_to_unit(c[0]), c16_to_unit(c[1]), c16_to_unit(c[2]), c16_to_unit(c[3]));
+        }
+        __syncthreads();
+    }
+}
+
+// Restore a plane to fp32 [B][H][T][D]. One CTA per (row chunk, h, b).
+template <int BS, int LAYOUT>
+__global__ void __launch_bounds__(kDecodeThreads) restore_plane_kernel(PlaneDev pl, int D, int T, int page_tokens,
+                                                                       const int32_t* table, int pps, int num_pages,
+                                                                       float* __restrict__ out, int32_t* status) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int CH = 8 * BS;
+    auto& scr = *reinterpret_cast<TileScratch<BS, LAYOUT>*>(smem);
+    float* tile = reinterpret_cast<float*>(smem + sizeof(TileScratch<BS, LAYOUT>));
+    const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+    const int t0 = blockIdx.x * CH;
+    const int rows = min(CH, T - t0);
+    SeqCtx sq{b, h, table, pps, num_pages, page_tokens, status};
+    decode_tile<BS, LAYOUT, true>(pl, sq, D, t0, rows, T, tile, D, scr);
+    float* dst = out + ((static_cast<int64_t>(b) * H + h) * T + t0) * D;
+    for (int i = threadIdx.x; i < rows * D; i += blockDim.x) dst[i] = tile[i];
+}
+
+// FP16 plane widened to fp32 [B][H][T][D].
+__global__ void restore_fp16_kernel(PlaneDev pl, int D, int T, int page_tokens, const int32_t* table, int pps,
+                                    int num_pages, float* __restrict__ out, int32_t* status) {
+    const int h = blockIdx.y, b = blockIdx.z, H = gridDim.y;
+    const int t = blockIdx.x;
+    const int phys = phys_page(table, pps, num_pages, b, t / page_tokens, status);
+    float* dst = out + ((static_cast<int64_t>(b) * H + h) * T + t) * D;
+    if (phys < 0) {
+        for (int c = threadIdx.x; c < D; c += blockDim.x) dst[c] = 0.f;
+        return;
+    }
+    const __half* row = reinterpret_cast<const __half*>(pl.data + b * pl.sB + h * pl.sH + static_cast<int64_t>(phys) * pl.sP) +
+                        static_cast<int64_t>(t % page_tokens) * D;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) dst[c] = __half2float(row[c]);
+}
+
+}  // namespace akv

@@ -1,0 +1,54 @@
+// TEST INFRASTRUCTURE ONLY. Compiles the product's device-side ASTC decoder
+// (astc-kv_b200/csrc/akv_astc_device.cuh) as plain host C++ so CPU tests can
+// compare its stage A/B logic with the oracle bit for bit before any GPU run.
+// Nothing in the product loads this library.
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+
+#define __device__
+#define __host__
+#define __forceinline__ inline
+#define __global__
+template <class T>
+inline T __ldg(const T* p) { return *p; }
+inline unsigned long long __brevll(unsigned long long x) {
+    unsigned long long r = 0;
+    for (int i = 0; i < 64; ++i) r |= ((x >> i) & 1ull) << (63 - i);
+    return r;
+}
+inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
+inline int __float_as_int(float f) { int i; std::memcpy(&i, &f, 4); return i; }
+struct uint4 { unsigned int x, y, z, w; };
+using std::max;
+using std::min;
+
+#include "../../astc-kv_b200/csrc/akv_astc_device.cuh"
+
+extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, uint16_t* out) {
+    static bool ready = false;
+    if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
+    const int fp = akv::footprint_index(bs);
+    if (fp < 0) return 1;
+    for (int64_t i = 0; i < n; ++i) {
+        uint4 b;
+        std::memcpy(&b, blocks + 16 * i, 16);
+        akv::BlockDesc<4> d;
+        uint8_t w[64];
+        std::memset(w, 0, sizeof(w));
+        akv::decode_header<4>(b, fp, d, w);
+        for (int y = 0; y < bs; ++y)
+            for (int x = 0; x < bs; ++x) {
+                uint32_t c[4];
+                switch (bs) {
+                    case 4: akv::texel_values<4, 4>(d, w, x, y, c); break;
+                    case 6: akv::texel_values<6, 4>(d, w, x, y, c); break;
+                    default: akv::texel_values<8, 4>(d, w, x, y, c); break;
+                }
+                for (int k = 0; k < 4; ++k) out[((i * bs + y) * bs + x) * 4 + k] = static_cast<uint16_t>(c[k]);
+            }
+    }
+    return 0;
+}
+
+extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
