@@ -61,6 +61,7 @@ class DevicePlane:
     side_stride_head: int = 0
     side_stride_page: int = 0
     kv_heads: int = 0
+    capacity_tokens: int = 0          # tokens per sequence a contiguous plane holds (0 = paged)
     keepalive: list = field(default_factory=list)
 
     def to_c(self) -> L.AkvPlane:
@@ -120,7 +121,7 @@ def contiguous_astc_plane(blocks: torch.Tensor, offsets: torch.Tensor, scales: t
     plane = DevicePlane("astc", blocks, H * T // block * cols * 16, T // block * cols * 16, page_bytes, block=block,
                         layout=layout, normalization=normalization, offsets=offsets, scales=scales,
                         meta_stride_batch=H * pages * mp, meta_stride_head=pages * mp, meta_stride_page=mp,
-                        kv_heads=H)
+                        kv_heads=H, capacity_tokens=T)
     if side is not None:
         S = side.shape[-1]
         plane.side, plane.side_channels = side, side_channels
@@ -136,7 +137,7 @@ def contiguous_fp16_plane(x: torch.Tensor, page_tokens: int) -> DevicePlane:
     assert x.dtype == torch.float16 and x.is_contiguous()
     if T % page_tokens:
         raise ValueError("tokens must be whole pages")
-    return DevicePlane("fp16", x, H * T * D * 2, T * D * 2, page_tokens * D * 2, kv_heads=H)
+    return DevicePlane("fp16", x, H * T * D * 2, T * D * 2, page_tokens * D * 2, kv_heads=H, capacity_tokens=T)
 
 
 def paged_astc_plane(atlas: torch.Tensor, offsets: torch.Tensor, scales: torch.Tensor, *, block: int, layout: str,
@@ -179,6 +180,13 @@ class Attention:
         d = L.AkvAttnDesc()
         d.batch, d.q_heads, d.head_dim = B, Hq, D
         d.kv_heads = self._kv_heads(k, v, Hq)
+        for pl in (k, v):
+            if block_table is None and pl.capacity_tokens and max_tokens > pl.capacity_tokens:
+                raise ValueError("max_tokens exceeds the tokens the contiguous plane holds")
+            if block_table is None and not pl.capacity_tokens:
+                raise ValueError("a paged plane needs a block table")
+            if block_table is not None and pl.capacity_tokens and pl.stride_batch:
+                raise ValueError("a contiguous plane cannot be addressed through a block table")
         d.max_tokens, d.page_tokens, d.split_tokens = max_tokens, page_tokens, split_tokens
         if q.dtype not in _Q_DTYPES or not q.is_contiguous():
             raise ValueError("q must be contiguous fp32/bf16/fp16 [B, Hq, D]")
@@ -218,6 +226,10 @@ class Attention:
     def run(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         L.check(L.lib().akv_cuda_decode_attention(self._dref, _stream_handle(stream)), "decode_attention")
         return self.out
+
+    def run_phase(self, phase: int, stream: torch.cuda.Stream | None = None) -> None:
+        """Issue only the split (1) or merge (2) launch; see akv_cuda_decode_attention_phase."""
+        L.check(L.lib().akv_cuda_decode_attention_phase(self._dref, phase, _stream_handle(stream)), "decode_attention")
 
 
 def decode_attention(q: torch.Tensor, k: DevicePlane, v: DevicePlane, **kw) -> torch.Tensor:
@@ -259,6 +271,8 @@ def restore_plane(plane: DevicePlane, *, batch: int, kv_heads: int, max_tokens: 
     """Decode + affine restore of a whole plane -> fp32 [B, H, T, D] (bit-exact
     with the reference's NumPy restore, codec.py:198-208)."""
     _require_cuda(plane.data, block_table)
+    if block_table is None and (not plane.capacity_tokens or max_tokens > plane.capacity_tokens):
+        raise ValueError("max_tokens exceeds the tokens the contiguous plane holds")
     out = torch.empty(batch, kv_heads, max_tokens, head_dim, dtype=torch.float32, device=plane.data.device)
     p = plane.to_c()
     bt = block_table.to(torch.int32).contiguous() if block_table is not None else None

@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
         // ASTC K tile.
         if constexpr (KBS > 0) {
             decode_tile<(KBS ? KBS : 4), AKV_LAYOUT_SCALAR, false>(p.k, sq, D, t0, n, t_end, k_s, D, kscr);
-            apply_side(p.k, sq, t0, n, t_end, k_s, D);
+            apply_side(p.k, sq, D, t0, n, t_end, k_s, D);
         }
         // 2. Scores.
         for (int base = warp * TPI; base < CH; base += (kAttnThreads / 32) * TPI) {

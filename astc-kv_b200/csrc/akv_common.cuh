@@ -164,7 +164,7 @@ __device__ __forceinline__ void decode_tile(const PlaneDev& pl, const SeqCtx& sq
 
 // Overwrite side-plane channels of a decoded K tile with their exact fp16
 // values.
-__device__ __forceinline__ void apply_side(const PlaneDev& pl, const SeqCtx& sq, int t0, int rows, int t_limit,
+__device__ __forceinline__ void apply_side(const PlaneDev& pl, const SeqCtx& sq, int D, int t0, int rows, int t_limit,
                                            float* tile, int ld) {
     if (pl.side_count <= 0) return;
     const int n = rows * pl.side_count;
@@ -176,6 +176,7 @@ __device__ __forceinline__ void apply_side(const PlaneDev& pl, const SeqCtx& sq,
         const int phys = phys_page(sq.table, sq.pps, sq.num_pages, sq.b, page, nullptr);
         if (phys < 0) continue;
         const int c = __ldg(pl.side_ch + sq.h * pl.side_count + j);
+        if (c < 0 || c >= D) continue;  // ids outside the head are ignored
         const __half* row = reinterpret_cast<const __half*>(pl.side + sq.b * pl.xB + sq.h * pl.xH +
                                                            static_cast<int64_t>(phys) * pl.xP) +
                             static_cast<int64_t>(t % sq.page_tokens) * pl.side_count;

@@ -74,7 +74,7 @@ bool valid_block(int b) { return b == 4 || b == 6 || b == 8; }
 // ---------------------------------------------------------------- attention
 
 template <int D, int G, int KBS, int VBS, int VL>
-int launch_attention(const AttnParams& p, cudaStream_t s) {
+int launch_attention(const AttnParams& p, cudaStream_t s, int phases) {
     using Cfg = AttnCfg<D, G, KBS, VBS, VL>;
     static_assert(Cfg::TG * G <= 2 * Cfg::CH || KBS == 0, "reduction fits");
     static_assert(Cfg::TG * G <= Cfg::CH, "reduction fits in the V tile");
@@ -84,17 +84,21 @@ int launch_attention(const AttnParams& p, cudaStream_t s) {
         cudaGetLastError();
         return AKV_ERR_CUDA;
     }
-    dim3 grid(p.nsplits, p.Hkv, p.B);
-    kern<<<grid, kAttnThreads, smem, s>>>(p);
-    int st = launch_status();
-    if (st) return st;
-    merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
-    return launch_status();
+    if (phases & AKV_PHASE_SPLIT) {
+        dim3 grid(p.nsplits, p.Hkv, p.B);
+        kern<<<grid, kAttnThreads, smem, s>>>(p);
+        if (int st = launch_status()) return st;
+    }
+    if (phases & AKV_PHASE_MERGE) {
+        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        if (int st = launch_status()) return st;
+    }
+    return AKV_OK;
 }
 
 int chunk_tokens(int kbs, int vbs) { return vbs ? 8 * vbs : (kbs ? 8 * kbs : 64); }
 
-using Launcher = int (*)(const AttnParams&, cudaStream_t);
+using Launcher = int (*)(const AttnParams&, cudaStream_t, int);
 
 struct Variant {
     int D, G, kbs, vbs, vl;
@@ -300,6 +304,11 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc) {
 }
 
 int akv_cuda_decode_attention(const AkvAttnDesc* d, void* stream) {
+    return akv_cuda_decode_attention_phase(d, AKV_PHASE_SPLIT | AKV_PHASE_MERGE, stream);
+}
+
+int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* stream) {
+    if (phase < AKV_PHASE_SPLIT || phase > (AKV_PHASE_SPLIT | AKV_PHASE_MERGE)) return AKV_ERR_INVALID_ARGUMENT;
     AttnPlan plan;
     if (int st = plan_attention(d, &plan)) return st;
     if (!d->q_dev || !d->out_dev) return AKV_ERR_INVALID_ARGUMENT;
@@ -321,7 +330,7 @@ int akv_cuda_decode_attention(const AkvAttnDesc* d, void* stream) {
     p.out = d->out_dev;
     p.status = d->status_dev;
     const Variant* v = find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl);
-    return v->fn(p, static_cast<cudaStream_t>(stream));
+    return v->fn(p, static_cast<cudaStream_t>(stream), phase);
 }
 
 int akv_cuda_restore_plane(const AkvPlane* plane, int32_t batch, int32_t kv_heads, int32_t max_tokens, int32_t head_dim,

@@ -149,6 +149,15 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc);
 
 int akv_cuda_decode_attention(const AkvAttnDesc* desc, void* stream);
 
+/* The two launches of akv_cuda_decode_attention issued one at a time, so a
+ * caller can place work or events between them: phase 1 writes the split
+ * partials (m, l, acc) to the workspace, phase 2 merges them into out.
+ * Calling phase 1 then phase 2 on one stream equals one
+ * akv_cuda_decode_attention call. */
+#define AKV_PHASE_SPLIT 1
+#define AKV_PHASE_MERGE 2
+int akv_cuda_decode_attention_phase(const AkvAttnDesc* desc, int phase, void* stream);
+
 /*
  * Restore a whole plane to fp32 [batch][kv_heads][max_tokens][head_dim]:
  * decode + affine, the device twin of EncodedTensor.decoded

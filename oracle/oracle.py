@@ -166,6 +166,8 @@ def attention_f64(q, k, v, lengths=None):
     out = np.zeros((b, hq, d))
     for i in range(b):
         n = t if lengths is None else int(lengths[i])
+        if n == 0:
+            continue  # empty sequence: the GPU path defines the output as 0
         qq = q[i].reshape(hk, hq // hk, d)
         s = np.einsum("hgd,htd->hgt", qq, k[i, :, :n]) * d ** -0.5
         s -= s.max(-1, keepdims=True)

@@ -1,0 +1,51 @@
+"""The product's device decoder (compiled for the host by tests/emu) against
+the oracle, bit for bit on the 16-bit interpolation result C."""
+import ctypes as ct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from common import golden
+from oracle import oracle as O
+
+EMU = Path(__file__).resolve().parent / "emu" / "_build" / "libakv_emu.so"
+
+
+def emu_decode(blocks, bs):
+    lib = ct.CDLL(str(EMU))
+    lib.emu_decode_blocks_u16.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int, ct.c_void_p]
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 16)
+    out = np.empty((b.shape[0], bs, bs, 4), np.uint16)
+    assert lib.emu_decode_blocks_u16(b.ctypes.data, b.shape[0], bs, out.ctypes.data) == 0
+    return out
+
+
+def test_golden_blocks():
+    g = golden("block_geometry_identity")
+    blocks = g["blocks"].reshape(-1, 16)
+    np.testing.assert_array_equal(emu_decode(blocks, 6), O.decode_blocks(blocks, 6, O.OUT_UNORM16, threads=4))
+
+
+@pytest.mark.parametrize("bs", [4, 6, 8])
+def test_random_legal_blocks(bs):
+    from astc_kv_cuda.ops import random_blocks
+    blocks = random_blocks(20000, bs, seed=1000 + bs)
+    np.testing.assert_array_equal(emu_decode(blocks, bs), O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
+
+
+@pytest.mark.parametrize("bs", [4, 6, 8])
+def test_random_bytes_including_illegal_encodings(bs):
+    blocks = np.random.default_rng(bs).integers(0, 256, (20000, 16), dtype=np.uint8)
+    np.testing.assert_array_equal(emu_decode(blocks, bs), O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
+
+
+def test_fp16_view_conversion_exhaustive():
+    lib = ct.CDLL(str(EMU))
+    lib.emu_unit.argtypes = [ct.c_uint32]
+    lib.emu_unit.restype = ct.c_float
+    L = O.lib()
+    for c in list(range(0, 70000, 7)) + [65535, 65534, 4, 3, 2047, 2048]:
+        c = min(c, 65535)
+        h = np.array([L.astc_oracle_unorm16_to_half(c)], np.uint16).view(np.float16)[0]
+        assert np.float32(h) == np.float32(lib.emu_unit(c)), c
