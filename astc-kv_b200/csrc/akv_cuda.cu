@@ -6,11 +6,13 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "../../include/akv_cuda.h"
 #include "akv_attention_kernels.cuh"
+#include "akv_attn_fast.cuh"
 #include "akv_decode_kernels.cuh"
 #include "akv_tables.h"
 
@@ -96,9 +98,92 @@ int launch_attention(const AttnParams& p, cudaStream_t s, int phases) {
     return AKV_OK;
 }
 
+using Launcher = int (*)(const AttnParams&, cudaStream_t, int);
+
+template <int D, int G, int VBS, int KBS>
+int launch_fast(const AttnParams& p, cudaStream_t s, int phases) {
+    using C = fast::Cfg<D, G, VBS, KBS>;
+    auto kern = fast::attn_fast_kernel<D, G, VBS, KBS>;
+    const size_t smem = sizeof(fast::Smem<D, G, VBS, KBS>);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return AKV_ERR_CUDA;
+    }
+    if (phases & AKV_PHASE_SPLIT) {
+        dim3 grid(p.nsplits, p.Hkv, p.B);
+        kern<<<grid, C::THREADS, smem, s>>>(p);
+        if (int st = launch_status()) return st;
+    }
+    if (phases & AKV_PHASE_MERGE) {
+        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        if (int st = launch_status()) return st;
+    }
+    return AKV_OK;
+}
+
+struct FastVariant {
+    int D, G, vbs, kbs;
+    Launcher fn;
+};
+
+// Tensor-core variants for scalar-layout ASTC V with FP16 (kbs 0) or scalar
+// ASTC K.
+#define AKV_FAST(D, G, VB, KB) {D, G, VB, KB, &launch_fast<D, G, VB, KB>}
+const FastVariant kFastVariants[] = {
+    AKV_FAST(64, 3, 6, 0), AKV_FAST(64, 3, 6, 6), AKV_FAST(64, 3, 4, 0), AKV_FAST(64, 3, 8, 0),
+    AKV_FAST(128, 4, 6, 0), AKV_FAST(128, 4, 4, 0), AKV_FAST(128, 4, 8, 0),
+    AKV_FAST(128, 8, 8, 4), AKV_FAST(128, 8, 8, 0), AKV_FAST(128, 8, 4, 0),
+};
+#undef AKV_FAST
+
+int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : 64; }
+
+const FastVariant* find_fast(int D, int G, int vbs, int kbs) {
+    for (const FastVariant& v : kFastVariants)
+        if (v.D == D && v.G == G && v.vbs == vbs && v.kbs == kbs) return &v;
+    return nullptr;
+}
+
+bool aligned16(int64_t bytes) { return bytes % 16 == 0; }
+
+// Metadata elements per chunk for a plane, and their offset granularity
+// inside a page (both must keep the bulk copies 16-byte aligned).
+bool meta_copy_ok(const AkvPlane& pl, int D, int CH) {
+    const int cols = (D + pl.block - 1) / pl.block;
+    int64_t elems, step;
+    if (pl.normalization == AKV_NORM_BLOCK_AFFINE) { elems = (CH / pl.block) * cols; step = elems; }
+    else if (pl.normalization == AKV_NORM_TOKEN) { elems = CH; step = CH; }
+    else { elems = D; step = 0; }
+    return aligned16(elems * 2) && aligned16(step * 2) && aligned16(pl.meta_stride_batch * 2) &&
+           aligned16(pl.meta_stride_head * 2) && aligned16(pl.meta_stride_page * 2) &&
+           reinterpret_cast<uintptr_t>(pl.offsets) % 16 == 0 && reinterpret_cast<uintptr_t>(pl.scales) % 16 == 0;
+}
+
+bool fast_path_ok(const AkvAttnDesc* d, int kbs, int vbs, int vl, int split) {
+    const char* env = std::getenv("AKV_ATTN_PATH");
+    if (env && std::strcmp(env, "generic") == 0) return false;
+    if (!vbs || vl != AKV_LAYOUT_SCALAR) return false;
+    if (d->k.storage == AKV_STORAGE_ASTC && d->k.layout != AKV_LAYOUT_SCALAR) return false;
+    if (!find_fast(d->head_dim, d->q_heads / d->kv_heads, vbs, kbs)) return false;
+    const int CH = fast_chunk(kbs, vbs);
+    if (d->page_tokens % CH || split % CH) return false;
+    const AkvPlane* planes[2] = {&d->k, &d->v};
+    for (const AkvPlane* pl : planes) {
+        if (!aligned16(pl->stride_batch) || !aligned16(pl->stride_head) || !aligned16(pl->stride_page)) return false;
+        if (pl->storage == AKV_STORAGE_ASTC && !meta_copy_ok(*pl, d->head_dim, CH)) return false;
+    }
+    if (d->k.side) {
+        if (d->k.side_count > 8) return false;
+        const int64_t sc2 = static_cast<int64_t>(d->k.side_count) * 2;
+        if (!aligned16(CH * sc2) || !aligned16(d->k.side_stride_batch) || !aligned16(d->k.side_stride_head) ||
+            !aligned16(d->k.side_stride_page) || reinterpret_cast<uintptr_t>(d->k.side) % 16)
+            return false;
+    }
+    return true;
+}
+
 int chunk_tokens(int kbs, int vbs) { return vbs ? 8 * vbs : (kbs ? 8 * kbs : 64); }
 
-using Launcher = int (*)(const AttnParams&, cudaStream_t, int);
 
 struct Variant {
     int D, G, kbs, vbs, vl;
@@ -135,6 +220,7 @@ const Variant* find_variant(int D, int G, int kbs, int vbs, int vl) {
 
 struct AttnPlan {
     int kbs, vbs, vl, split, nsplits;
+    bool fast;
     size_t ws;
 };
 
@@ -174,7 +260,9 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
     out->vbs = fps[1];
     out->vl = d->v.storage == AKV_STORAGE_ASTC ? d->v.layout : AKV_LAYOUT_SCALAR;
     if (!find_variant(d->head_dim, d->q_heads / d->kv_heads, out->kbs, out->vbs, out->vl)) return AKV_ERR_UNSUPPORTED;
-    const int ch = chunk_tokens(out->kbs, out->vbs);
+    const bool fast_shape = out->vbs && out->vl == AKV_LAYOUT_SCALAR &&
+                            find_fast(d->head_dim, d->q_heads / d->kv_heads, out->vbs, out->kbs);
+    const int ch = fast_shape ? fast_chunk(out->kbs, out->vbs) : chunk_tokens(out->kbs, out->vbs);
     int split = d->split_tokens;
     if (split <= 0) {
         // Enough (split, head, batch) units for ~8 CTAs per SM.
@@ -193,6 +281,7 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
     if (split % lcm_fp) return AKV_ERR_INVALID_ARGUMENT;
     out->split = split;
     out->nsplits = (d->max_tokens + split - 1) / split;
+    out->fast = fast_path_ok(d, out->kbs, out->vbs, out->vl, split);
     out->ws = static_cast<size_t>(d->batch) * d->q_heads * out->nsplits * (d->head_dim + 2) * sizeof(float);
     return AKV_OK;
 }
@@ -242,6 +331,7 @@ const char* akv_cuda_error(int code) {
         case AKV_ERR_NOT_INITIALIZED: return "decode tables not initialised on this device (call akv_cuda_init outside stream capture)";
         case AKV_ERR_BAD_BLOCK_TABLE: return "block table entry outside [0, num_pages)";
         case AKV_ERR_WORKSPACE: return "workspace missing or smaller than akv_cuda_attention_workspace()";
+        case AKV_ERR_TIMEOUT: return "a kernel's bounded wait for its own asynchronous copies ran out";
         default: return "unknown status code";
     }
 }
@@ -329,6 +419,10 @@ int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* strea
     p.part_ml = ws + static_cast<size_t>(d->batch) * d->q_heads * plan.nsplits * d->head_dim;
     p.out = d->out_dev;
     p.status = d->status_dev;
+    if (plan.fast) {
+        const FastVariant* f = find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs);
+        return f->fn(p, static_cast<cudaStream_t>(stream), phase);
+    }
     const Variant* v = find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl);
     return v->fn(p, static_cast<cudaStream_t>(stream), phase);
 }

@@ -31,6 +31,7 @@ extern "C" {
 #define AKV_ERR_NOT_INITIALIZED 4    /* akv_cuda_init has not run on this device and could not run now */
 #define AKV_ERR_BAD_BLOCK_TABLE 5    /* a kernel saw a block-table entry outside [0, num_pages) */
 #define AKV_ERR_WORKSPACE 6          /* workspace missing or smaller than akv_cuda_attention_workspace() */
+#define AKV_ERR_TIMEOUT 7            /* a kernel's bounded wait for its own async copies ran out */
 
 /* Decoder output views of the 16-bit interpolation result C of each texel. */
 #define AKV_OUT_UNORM8 0   /* C >> 8 (decode_unorm8), 4 bytes per texel */
