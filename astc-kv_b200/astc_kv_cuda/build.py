@@ -20,7 +20,8 @@ INCLUDE = ROOT.parent / "include"
 LIB = PKG / "libakv_cuda.so"
 
 SOURCES = ["akv_cuda.cu", "akv_tables.cpp", "akv_encode.cpp"]
-HEADERS = ["akv_astc_device.cuh", "akv_common.cuh", "akv_decode_kernels.cuh", "akv_attention_kernels.cuh", "akv_tables.h"]
+HEADERS = ["akv_astc_device.cuh", "akv_common.cuh", "akv_decode_kernels.cuh", "akv_attention_kernels.cuh", "akv_tables.h",
+           "akv_attn_fast.cuh", "akv_decode_fast.cuh"]
 
 
 def nvcc() -> str:

@@ -7,15 +7,14 @@
 //   * Staging: one elected thread issues cp.async.bulk copies of the chunk's
 //     V blocks and fp16 metadata (and ASTC K blocks) into a two-stage shared
 //     ring, completed on mbarriers; consumers wait with a bounded try_wait.
-//   * Decode, stage A (thread per block): header, endpoints and weight codes.
-//     For the common block kinds (single weight plane, full-resolution grid)
-//     the block becomes a value table u[partition][weight code] (exact fp16
-//     values of the decoded texels) plus one index byte per texel; other
-//     blocks (reduced grids with infill, dual plane) store one table entry per
-//     texel with identity indices, so stage B is uniform.
-//   * Decode, stage B (thread per block row of texels): u = table[index],
-//     v = scale*u + offset, split into fp16 hi + lo parts, written to padded
-//     [token][channel] tiles.
+//   * Decode (decode_plane_sorted): blocks are classified and counting-sorted
+//     by class so a warp's lanes share one code path; fast classes (single
+//     weight plane, full-resolution grid; akv_decode_fast.cuh) become a
+//     value table per block plus one index byte per texel, reduced-grid and
+//     dual-plane blocks get per-texel table entries computed one thread per
+//     texel. Table entries already hold v = scale*u + offset split into fp16
+//     hi and lo for block-affine planes. A thread per block row of texels
+//     then writes the padded [token][channel] hi/lo tiles.
 //   * Tensor cores (mma.sync m16n8k16, fp32 accumulation), one warp per 16
 //     tokens of the chunk, query heads of the GQA group as the N=8 dimension:
 //       S^T[tok][head] = K . Q^T   (q hi+lo; K fp16 straight from global
@@ -32,6 +31,7 @@
 
 #include "akv_attention_kernels.cuh"
 #include "akv_common.cuh"
+#include "akv_decode_fast.cuh"
 
 namespace akv {
 namespace fast {
@@ -120,141 +120,162 @@ __device__ __forceinline__ void split_pair(float v0, float v1, uint32_t& hi, uin
     lo = pack_h2(v0 - hf.x, v1 - hf.y);
 }
 
-// ------------------------------------------------------------------ decode
-
-// Stage A of the fast path for one block (R channel of a scalar-layout
-// plane). Writes `tab` (fp16 u values) and `idx` (per-texel table index).
+// Bytes of metadata per chunk for a plane.
 template <int BS>
-__device__ __forceinline__ void decode_block_table(uint4 blk, __half* tab, uint8_t* idx) {
-    constexpr int fp = footprint_index(BS);
+__device__ __forceinline__ int meta_elems(int norm, int cols, int CH, int D) {
+    return norm == AKV_NORM_BLOCK_AFFINE ? (CH / BS) * cols : (norm == AKV_NORM_TOKEN ? CH : D);
+}
+
+template <int BS>
+__device__ __forceinline__ int64_t meta_chunk_offset(int norm, int cols, int t_in_page) {
+    return norm == AKV_NORM_BLOCK_AFFINE ? static_cast<int64_t>(t_in_page / BS) * cols
+                                         : (norm == AKV_NORM_TOKEN ? t_in_page : 0);
+}
+
+// Scratch of the sorted decode for one plane-chunk of up to NB blocks.
+template <int NB, int TEX>
+struct DecodeScratch {
+    uint32_t tab[NB][TEX];
+    uint32_t idx[NB][(TEX + 3) / 4];
+    uint16_t order[NB];
+    uint8_t cls[NB];
+    int count[kNumCls];
+    int base[kNumCls];
+    int nslow;
+};
+
+// Per-texel scratch of slow blocks (aliases the tiles, which are free while
+// a chunk is being decoded).
+template <int NB>
+struct SlowScratch {
+    static constexpr int kCap = NB < 96 ? NB : 96;  // fits in the two tiles of every variant
+    BlockDesc<1> desc[kCap];
+    uint8_t w[kCap][64];
+};
+
+// Decode one plane's chunk into the hi/lo tiles. All threads call it.
+template <int BS, int D, int THREADS, int NB, int LD>
+__device__ __forceinline__ void decode_plane_sorted(const uint4* raw, const __half* moff, const __half* mscl, int norm,
+                                                    int cols, int rows_blk, int n, bool valid,
+                                                    DecodeScratch<NB, BS * BS>& ds, SlowScratch<NB>& ss,
+                                                    __half (*thi)[LD], __half (*tlo)[LD]) {
     constexpr int N = BS * BS;
-    const Tables& T = g_akv_tables;
-    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
-    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
-    const int mode = static_cast<int>(lo & 0x7FF);
-    auto constant = [&](float u) {
-        tab[0] = __float2half_rn(u);  // exact: u is an fp16 value
-#pragma unroll
-        for (int t = 0; t < N; t += 4) *reinterpret_cast<uint32_t*>(idx + t) = 0u;
-    };
-    const uint32_t me = __ldg(&T.mode[fp][mode]);
-    const int parts = static_cast<int>((lo >> 11) & 3) + 1;
-    const bool fast_kind = (me & kModeValid) && !(me & kModeDual) && !(me & kModeReduced);
-    if (!fast_kind || (mode & 0x1FF) == 0x1FC) {
-        // Void extent, error, reduced grid or dual plane: per-texel values.
-        BlockDesc<1> d;
-        uint8_t w[64];
+    constexpr int fp = footprint_index(BS);
+    const int nblk = rows_blk * cols;
+    const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
+    // Phase 0: classify and count.
+    if (threadIdx.x < kNumCls) ds.count[threadIdx.x] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nblk; i += THREADS) {
+        const int c = classify<BS>(raw[i]);
+        ds.cls[i] = static_cast<uint8_t>(c);
+        atomicAdd(&ds.count[c], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int c = 0; c < kNumCls; ++c) { ds.base[c] = acc; acc += ds.count[c]; }
+        ds.nslow = ds.count[kClsSlow];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nblk; i += THREADS) {
+        const int c = ds.cls[i];
+        ds.order[atomicAdd(&ds.base[c], 1)] = static_cast<uint16_t>(i);
+    }
+    __syncthreads();
+    // Phase 1: class-ordered block decode.
+    const int s0 = ds.base[kClsSlow] - ds.count[kClsSlow];  // first slow block in `order`
+    for (int k = threadIdx.x; k < nblk; k += THREADS) {
+        const int i = ds.order[k];
+        const int c = ds.cls[i];
+        const uint4 blk = raw[i];
+        const float sc = affine ? __half2float(mscl[i]) : 0.f;
+        const float of = affine ? __half2float(moff[i]) : 0.f;
+        uint32_t* tab = ds.tab[i];
+        if (c >= kClsFast) {
+            decode_fast_any<BS>(c - kClsFast, blk, affine, sc, of, tab, reinterpret_cast<uint8_t*>(ds.idx[i]));
+            continue;
+        }
+        const int slot = k - s0;
+        const bool scratch = c == kClsSlow && slot < SlowScratch<NB>::kCap;
+        BlockDesc<1> dl;
+        uint8_t wl[64];
+        BlockDesc<1>& d = scratch ? ss.desc[slot] : dl;
+        uint8_t* w = scratch ? ss.w[slot] : wl;
         decode_header<1>(blk, fp, d, w);
-        if (d.info & ((1u << kInfoVoid) | (1u << kInfoError))) {
-            uint32_t c[1];
-            texel_values<BS, 1>(d, w, 0, 0, c);
-            constant(c16_to_unit(c[0]));
-            return;
-        }
-#pragma unroll 1
-        for (int t = 0; t < N; ++t) {
-            uint32_t c[1];
-            texel_values<BS, 1>(d, w, t % BS, t / BS, c);
-            tab[t] = __float2half_rn(c16_to_unit(c[0]));
-            idx[t] = static_cast<uint8_t>(t);
-        }
-        return;
-    }
-    const int wq = mode_wq(me), wbits = mode_wbits(me);
-    const int top = 128 - wbits;
-    int cem[4];
-    int cstart, extra = 0, seed = 0;
-    if (parts == 1) {
-        cem[0] = static_cast<int>((lo >> 13) & 15);
-        cstart = 17;
-    } else {
-        seed = static_cast<int>((lo >> 13) & 0x3FF);
-        const int field = static_cast<int>((lo >> 23) & 0x3F);
-        cstart = 29;
-        if ((field & 3) == 0) {
+        if (c == kClsConst || (d.info & ((1u << kInfoVoid) | (1u << kInfoError)))) {
+            uint32_t cv[1];
+            texel_values<BS, 1>(d, w, 0, 0, cv);
+            tab[0] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
 #pragma unroll
-            for (int p = 0; p < 4; ++p) cem[p] = field >> 2;
-        } else {
-            extra = 3 * parts - 4;
-            const int all = (field >> 2) | (static_cast<int>(bits_u128(lo, hi, top - extra, extra)) << 4);
-            const int cls = (field & 3) - 1;
+            for (int t = 0; t < (N + 3) / 4; ++t) ds.idx[i][t] = 0u;
+            ds.cls[i] = kClsConst;
+            continue;
+        }
 #pragma unroll
-            for (int p = 0; p < 4; ++p) cem[p] = ((cls + ((all >> p) & 1)) << 2) | ((all >> (parts + 2 * p)) & 3);
-        }
-    }
-    int npairs = 0;
-    for (int p = 0; p < parts; ++p) npairs += (cem[p] >> 2) + 1;
-    const int avail = top - extra - cstart;
-    const int cq = (npairs <= 9 && avail >= 0) ? T.cquant[npairs][avail] : 0xFF;
-    const uint32_t wshape = __ldg(&T.shape[wq]);
-    const int levels = (1 << (wshape & 15)) * ((wshape >> 4) & 1 ? 3 : ((wshape >> 5) & 1 ? 5 : 1));
-    if (cq == 0xFF || parts * levels > N) {
-        // Illegal colour budget, or a table larger than the block: per texel.
-        BlockDesc<1> d;
-        uint8_t w[64];
-        decode_header<1>(blk, fp, d, w);
-        if (d.info & ((1u << kInfoVoid) | (1u << kInfoError))) {
-            uint32_t c[1];
-            texel_values<BS, 1>(d, w, 0, 0, c);
-            constant(c16_to_unit(c[0]));
-            return;
-        }
+        for (int t = 0; t < N; t += 4) ds.idx[i][t / 4] = t | ((t + 1) << 8) | ((t + 2) << 16) | ((t + 3) << 24);
+        if (!scratch) {
+            // Beyond the scratch capacity: evaluate the texels here.
 #pragma unroll 1
-        for (int t = 0; t < N; ++t) {
-            uint32_t c[1];
-            texel_values<BS, 1>(d, w, t % BS, t / BS, c);
-            tab[t] = __float2half_rn(c16_to_unit(c[0]));
-            idx[t] = static_cast<uint8_t>(t);
-        }
-        return;
-    }
-    // Colour integers -> R endpoints per partition.
-    int vals[18];
-    {
-        uint64_t clo = window_u128(lo, hi, cstart);
-        uint64_t chi = hi >> cstart;
-        mask_u128(clo, chi, bise_stream_bits_dev(2 * npairs, cq));
-        bise_stream(clo, chi, 2 * npairs, cq, [&](int i, int code) { vals[i] = __ldg(&T.cunq[cq][code]); });
-    }
-    int e0[4], e1[4];
-    {
-        int k = 0;
-#pragma unroll 1
-        for (int p = 0; p < parts; ++p) {
-            int a[4], b[4];
-            if (!endpoints(cem[p], vals + k, a, b)) {
-                constant(1.0f);  // HDR endpoint mode in the LDR profile: error colour (R = 1)
-                return;
+            for (int t = 0; t < N; ++t) {
+                uint32_t cv[1];
+                texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
+                tab[t] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
             }
-            e0[p] = a[0];
-            e1[p] = b[0];
-            k += 2 * ((cem[p] >> 2) + 1);
         }
     }
-    // Value table u[p * levels + code].
-#pragma unroll 1
-    for (int p = 0; p < parts; ++p)
-#pragma unroll 1
-        for (int code = 0; code < levels; ++code) {
-            const int w = __ldg(&T.wunq[wq][code]);
-            const int X = e0[p] * (64 - w) + e1[p] * w;
-            tab[p * levels + code] = __float2half_rn(c16_to_unit(static_cast<uint32_t>(4 * X + ((X + 32) >> 6))));
+    __syncthreads();
+    // Phase 1b: texels of slow blocks held in the scratch, thread per texel.
+    const int nscr = min(ds.nslow, SlowScratch<NB>::kCap);
+    if (nscr > 0) {
+        const int ntex = nscr * N;
+        for (int k = threadIdx.x; k < ntex; k += THREADS) {
+            const int slot = k / N;
+            const int i = ds.order[s0 + slot];
+            if (ds.cls[i] != kClsSlow) continue;  // turned out constant
+            const int t = k - slot * N;
+            uint32_t cv[1];
+            texel_values<BS, 1>(ss.desc[slot], ss.w[slot], t % BS, t / BS, cv);
+            const float sc = affine ? __half2float(mscl[i]) : 0.f;
+            const float of = affine ? __half2float(moff[i]) : 0.f;
+            ds.tab[i][t] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
         }
-    // Per-texel index: partition * levels + weight code (full grid: weight i = texel i).
-    uint32_t pat[4] = {0u, 0u, 0u, 0u};
-    if (parts > 1) {
-        const uint32_t* pt = T.part[fp][parts - 2][seed];
-        pat[0] = __ldg(pt + 0);
-        pat[1] = __ldg(pt + 1);
-        pat[2] = __ldg(pt + 2);
-        pat[3] = __ldg(pt + 3);
+        __syncthreads();
     }
-    uint64_t wlo = __brevll(hi), whi = __brevll(lo);
-    mask_u128(wlo, whi, wbits);
-    bise_stream(wlo, whi, N, wq, [&](int i, int code) {
-        const int part = (pat[i >> 4] >> (2 * (i & 15))) & 3;
-        idx[i] = static_cast<uint8_t>(part * levels + code);
-    });
+    // Phase 2: tiles, thread per (block, texel row).
+    const int ntask = nblk * BS;
+    for (int task = threadIdx.x; task < ntask; task += THREADS) {
+        const int bi = task / BS, y = task - bi * BS;
+        const int br = bi / cols, bc = bi - br * cols;
+        const int row = br * BS + y;
+        const bool ok = valid && row < n;
+        const uint8_t* ix = reinterpret_cast<const uint8_t*>(ds.idx[bi]) + y * BS;
+        const uint32_t* tb = ds.tab[bi];
+        float tsc = 0.f, tof = 0.f;
+        if (norm == AKV_NORM_TOKEN) { tsc = __half2float(mscl[row]); tof = __half2float(moff[row]); }
+#pragma unroll
+        for (int x = 0; x < BS; x += 2) {
+            const int col = bc * BS + x;
+            if (col >= D) break;
+            const uint32_t a = tb[ix[x]], b2 = tb[ix[x + 1]];
+            uint32_t h, l;
+            if (affine) {
+                h = __byte_perm(a, b2, 0x5410);
+                l = __byte_perm(a, b2, 0x7632);
+            } else {
+                float s0 = tsc, o0 = tof, s1 = tsc, o1 = tof;
+                if (norm == AKV_NORM_PAGE_CHANNEL) {
+                    s0 = __half2float(mscl[col]); o0 = __half2float(moff[col]);
+                    s1 = __half2float(mscl[col + 1]); o1 = __half2float(moff[col + 1]);
+                }
+                split_pair(fmaf(__uint_as_float(a), s0, o0), fmaf(__uint_as_float(b2), s1, o1), h, l);
+            }
+            if (!ok) { h = 0u; l = 0u; }
+            *reinterpret_cast<uint32_t*>(&thi[row][col]) = h;
+            *reinterpret_cast<uint32_t*>(&tlo[row][col]) = l;
+        }
+    }
+    __syncthreads();
 }
 
 // ------------------------------------------------------------------ kernel
@@ -274,8 +295,10 @@ struct Cfg {
     static constexpr int META = (VBLK > CH ? (VBLK > D ? VBLK : D) : (CH > D ? CH : D));
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
-    static constexpr int SCR = THREADS;                        // blocks decoded per pass
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
+    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, VBS * VBS>);
+    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), KBS * KBS>) : 0;
+    static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
 };
@@ -294,69 +317,11 @@ struct Smem {
     __align__(16) __half vlo[C::CH][C::LD];
     __align__(16) __half khi[KBS ? C::CH : 1][C::LD];
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
-    __align__(16) __half tab[C::SCR][C::MAXBS * C::MAXBS];
-    __align__(16) uint8_t idx[C::SCR][C::MAXBS * C::MAXBS];
+    __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[C::NWM][8][16];
     float wm[C::NWM][8];
     float wl[C::NWM][8];
 };
-
-// Bytes of metadata per chunk for a plane.
-template <int BS>
-__device__ __forceinline__ int meta_elems(int norm, int cols, int CH, int D) {
-    return norm == AKV_NORM_BLOCK_AFFINE ? (CH / BS) * cols : (norm == AKV_NORM_TOKEN ? CH : D);
-}
-
-template <int BS>
-__device__ __forceinline__ int64_t meta_chunk_offset(int norm, int cols, int t_in_page) {
-    return norm == AKV_NORM_BLOCK_AFFINE ? static_cast<int64_t>(t_in_page / BS) * cols
-                                         : (norm == AKV_NORM_TOKEN ? t_in_page : 0);
-}
-
-// Decode the chunk's blocks of one plane (from the staged raw blocks) into the
-// hi/lo tiles. All threads call it.
-template <int BS, int D, int THREADS, int SCRN, int TABN, int LD>
-__device__ __forceinline__ void decode_plane_chunk(const uint4* raw, const __half* moff, const __half* mscl, int norm,
-                                                   int cols, int rows_blk, int n, bool valid,
-                                                   __half (*tab)[TABN], uint8_t (*idx)[TABN],
-                                                   __half (*thi)[LD], __half (*tlo)[LD]) {
-    const int nblk = rows_blk * cols;
-    for (int pass = 0; pass < nblk; pass += SCRN) {
-        const int nb = min(SCRN, nblk - pass);
-        for (int i = threadIdx.x; i < nb; i += THREADS) decode_block_table<BS>(raw[pass + i], tab[i], idx[i]);
-        __syncthreads();
-        const int ntask = nb * BS;
-        for (int task = threadIdx.x; task < ntask; task += THREADS) {
-            const int li = task / BS, y = task - li * BS;
-            const int bi = pass + li;
-            const int br = bi / cols, bc = bi - br * cols;
-            const int row = br * BS + y;
-            const bool ok = valid && row < n;
-            float sc = 0.f, of = 0.f;
-            if (norm == AKV_NORM_BLOCK_AFFINE) { sc = __half2float(mscl[bi]); of = __half2float(moff[bi]); }
-            else if (norm == AKV_NORM_TOKEN) { sc = __half2float(mscl[row]); of = __half2float(moff[row]); }
-            const uint8_t* ix = idx[li] + y * BS;
-            const __half* tb = tab[li];
-#pragma unroll
-            for (int x = 0; x < BS; x += 2) {
-                const int col = bc * BS + x;
-                if (col >= D) break;
-                float s0 = sc, o0 = of, s1 = sc, o1 = of;
-                if (norm == AKV_NORM_PAGE_CHANNEL) {
-                    s0 = __half2float(mscl[col]); o0 = __half2float(moff[col]);
-                    s1 = __half2float(mscl[col + 1]); o1 = __half2float(moff[col + 1]);
-                }
-                const float v0 = ok ? fmaf(__half2float(tb[ix[x]]), s0, o0) : 0.f;
-                const float v1 = ok ? fmaf(__half2float(tb[ix[x + 1]]), s1, o1) : 0.f;
-                uint32_t h, l;
-                split_pair(v0, v1, h, l);
-                *reinterpret_cast<uint32_t*>(&thi[row][col]) = h;
-                *reinterpret_cast<uint32_t*>(&tlo[row][col]) = l;
-            }
-        }
-        __syncthreads();
-    }
-}
 
 template <int D, int G, int VBS, int KBS>
 __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_kernel(AttnParams p) {
@@ -516,13 +481,18 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
         }
         const bool valid = sm.valid[s] != 0;
         // Decode V (and K) tiles.
-        decode_plane_chunk<VBS, D, THREADS, C::SCR, C::MAXBS * C::MAXBS, LD>(
-            sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS, CH / VBS, n, valid, sm.tab, sm.idx,
-            sm.vhi, sm.vlo);
+        auto& slow = *reinterpret_cast<SlowScratch<C::VBLK>*>(&sm.vhi[0][0]);
+        decode_plane_sorted<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
+                                                         C::VCOLS, CH / VBS, n, valid,
+                                                         *reinterpret_cast<DecodeScratch<C::VBLK, VBS * VBS>*>(sm.ds),
+                                                         slow, sm.vhi, sm.vlo);
         if constexpr (KBS > 0) {
-            decode_plane_chunk<(KBS ? KBS : 4), D, THREADS, C::SCR, C::MAXBS * C::MAXBS, LD>(
-                sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS, CH / KBS, n, valid, sm.tab, sm.idx,
-                sm.khi, sm.klo);
+            constexpr int KB = KBS ? KBS : 4;
+            constexpr int KN = KBS ? C::KBLK : 1;
+            auto& kslow = *reinterpret_cast<SlowScratch<KN>*>(&sm.khi[0][0]);
+            decode_plane_sorted<KB, D, THREADS, KN, LD>(
+                sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS, CH / KB, n, valid,
+                *reinterpret_cast<DecodeScratch<KN, KB * KB>*>(sm.ds), kslow, sm.khi, sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;
             if (sc > 0) {

@@ -124,11 +124,12 @@ int launch_fast(const AttnParams& p, cudaStream_t s, int phases) {
 struct FastVariant {
     int D, G, vbs, kbs;
     Launcher fn;
+    size_t smem;
 };
 
 // Tensor-core variants for scalar-layout ASTC V with FP16 (kbs 0) or scalar
 // ASTC K.
-#define AKV_FAST(D, G, VB, KB) {D, G, VB, KB, &launch_fast<D, G, VB, KB>}
+#define AKV_FAST(D, G, VB, KB) {D, G, VB, KB, &launch_fast<D, G, VB, KB>, sizeof(fast::Smem<D, G, VB, KB>)}
 const FastVariant kFastVariants[] = {
     AKV_FAST(64, 3, 6, 0), AKV_FAST(64, 3, 6, 6), AKV_FAST(64, 3, 4, 0), AKV_FAST(64, 3, 8, 0),
     AKV_FAST(128, 4, 6, 0), AKV_FAST(128, 4, 4, 0), AKV_FAST(128, 4, 8, 0),
@@ -164,7 +165,15 @@ bool fast_path_ok(const AkvAttnDesc* d, int kbs, int vbs, int vl, int split) {
     if (env && std::strcmp(env, "generic") == 0) return false;
     if (!vbs || vl != AKV_LAYOUT_SCALAR) return false;
     if (d->k.storage == AKV_STORAGE_ASTC && d->k.layout != AKV_LAYOUT_SCALAR) return false;
-    if (!find_fast(d->head_dim, d->q_heads / d->kv_heads, vbs, kbs)) return false;
+    const FastVariant* fv = find_fast(d->head_dim, d->q_heads / d->kv_heads, vbs, kbs);
+    if (!fv) return false;
+    int dev = 0, smem_max = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        fv->smem > static_cast<size_t>(smem_max)) {
+        cudaGetLastError();
+        return false;
+    }
     const int CH = fast_chunk(kbs, vbs);
     if (d->page_tokens % CH || split % CH) return false;
     const AkvPlane* planes[2] = {&d->k, &d->v};

@@ -58,6 +58,17 @@ def dist_env():
     return world, rank, local
 
 
+def reduce_max(values: list[float], world: int, device=None) -> list[float]:
+    """Element-wise max over ranks (timing: the slowest rank defines a step)."""
+    if world <= 1:
+        return list(values)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -339,11 +350,9 @@ def run_ours(args) -> dict | None:
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    times = torch.tensor([total_ms, e2e_ms, split_ms], dtype=torch.float64, device=dev)
+    total_ms, e2e_ms, split_ms = reduce_max([total_ms, e2e_ms, split_ms], world, dev)
     if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
-    total_ms, e2e_ms, split_ms = times.tolist()
     if rank != 0:
         return None
     hbm, hbm_src = peaks()

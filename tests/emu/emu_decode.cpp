@@ -5,6 +5,8 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <cmath>
+#include <vector_types.h>
 
 #define __device__
 #define __host__
@@ -19,11 +21,16 @@ inline unsigned long long __brevll(unsigned long long x) {
 }
 inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
 inline int __float_as_int(float f) { int i; std::memcpy(&i, &f, 4); return i; }
-struct uint4 { unsigned int x, y, z, w; };
 using std::max;
 using std::min;
 
+#include <cuda_fp16.h>
+#include <cmath>
+using std::fmaf;
+inline float __uint_as_float(unsigned int i) { float f; std::memcpy(&f, &i, 4); return f; }
+inline unsigned int __float_as_uint(float f) { unsigned int i; std::memcpy(&i, &f, 4); return i; }
 #include "../../astc-kv_b200/csrc/akv_astc_device.cuh"
+#include "../../astc-kv_b200/csrc/akv_decode_fast.cuh"
 
 extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, uint16_t* out) {
     static bool ready = false;
@@ -52,3 +59,26 @@ extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, u
 }
 
 extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
+
+// The fast per-block path of the sorted decode: class, then (for fast
+// classes) table + indices; returns the fp16-view values of the R channel
+// per texel, or -1 in cls for blocks that take the per-texel path.
+extern "C" int emu_decode_fast_r(const uint8_t* blocks, int64_t n, int bs, float* out, int* cls) {
+    static bool ready = false;
+    if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
+    for (int64_t i = 0; i < n; ++i) {
+        uint4 b;
+        std::memcpy(&b, blocks + 16 * i, 16);
+        int c = bs == 4 ? akv::fast::classify<4>(b) : bs == 6 ? akv::fast::classify<6>(b) : akv::fast::classify<8>(b);
+        cls[i] = c;
+        const int N = bs * bs;
+        if (c < akv::fast::kClsFast) { for (int t = 0; t < N; ++t) out[i * N + t] = -1.f; continue; }
+        uint32_t tab[64];
+        uint8_t idx[64];
+        if (bs == 4) akv::fast::decode_fast_any<4>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
+        else if (bs == 6) akv::fast::decode_fast_any<6>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
+        else akv::fast::decode_fast_any<8>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
+        for (int t = 0; t < N; ++t) out[i * N + t] = __uint_as_float(tab[idx[t]]);
+    }
+    return 0;
+}

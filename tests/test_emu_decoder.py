@@ -49,3 +49,39 @@ def test_fp16_view_conversion_exhaustive():
         c = min(c, 65535)
         h = np.array([L.astc_oracle_unorm16_to_half(c)], np.uint16).view(np.float16)[0]
         assert np.float32(h) == np.float32(lib.emu_unit(c)), c
+
+
+def emu_fast_r(blocks, bs):
+    lib = ct.CDLL(str(EMU))
+    lib.emu_decode_fast_r.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int, ct.c_void_p, ct.c_void_p]
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 16)
+    out = np.empty((b.shape[0], bs * bs), np.float32)
+    cls = np.empty(b.shape[0], np.int32)
+    assert lib.emu_decode_fast_r(b.ctypes.data, b.shape[0], bs, out.ctypes.data, cls.ctypes.data) == 0
+    return out, cls
+
+
+@pytest.mark.parametrize("source", ["golden", "random", "garbage", "encoder"])
+@pytest.mark.parametrize("bs", [4, 6, 8])
+def test_fast_table_decode_matches_oracle(source, bs):
+    """The attention kernel's per-block value-table decode (fast classes:
+    single weight plane, full-resolution grid) against the oracle's fp16 view."""
+    from astc_kv_cuda.ops import host_encode, random_blocks
+    if source == "golden":
+        if bs != 6:
+            pytest.skip("the reference's goldens are 6x6")
+        blocks = golden("block_geometry_identity")["blocks"].reshape(-1, 16)
+    elif source == "random":
+        blocks = random_blocks(20000, bs, seed=50 + bs)
+    elif source == "garbage":
+        blocks = np.random.default_rng(60 + bs).integers(0, 256, (20000, 16), dtype=np.uint8)
+    else:
+        x = np.random.default_rng(bs).random((bs * 20, bs * 22), np.float32)
+        x = np.repeat(x[..., None], 4, -1)
+        x[..., 3] = 1
+        blocks = np.frombuffer(host_encode(x, bs, "scalar", 1), np.uint8).reshape(-1, 16)
+    got, cls = emu_fast_r(blocks, bs)
+    ref = O.decode_blocks(blocks, bs, O.OUT_FP16, threads=4)[..., 0].reshape(len(got), bs * bs).astype(np.float32)
+    fast = cls >= 2
+    assert fast.any()
+    np.testing.assert_array_equal(got[fast], ref[fast])
