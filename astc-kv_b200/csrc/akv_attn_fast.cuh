@@ -86,6 +86,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// 16-byte global -> shared asynchronous copy (LDGSTS), completed by
+// cp.async.wait_group.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
     asm volatile(
@@ -319,12 +327,14 @@ struct Smem {
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[C::NWM][8][16];
+    __align__(16) uint4 qfrag[D / 16][32];                         // per lane: q hi (2 words) | q lo (2 words)
+    __align__(16) uint4 kstage[KBS ? 1 : C::NWM][2][KBS ? 1 : D / 32][32];  // FP16 K fragments per MMA warp
     float wm[C::NWM][8];
     float wl[C::NWM][8];
 };
 
 template <int D, int G, int VBS, int KBS>
-__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_kernel(AttnParams p) {
+__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_kernel(AttnParams p) {
     using C = Cfg<D, G, VBS, KBS>;
     using S = Smem<D, G, VBS, KBS>;
     constexpr int CH = C::CH, NWM = C::NWM, THREADS = C::THREADS, LD = C::LD;
@@ -416,11 +426,11 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
         if (nchunks > 1) issue(1, 1);
     }
 
-    // Query fragments (B operand, hi + lo), heads n = lane/4 of the group.
+    // Query fragments (B operand, hi + lo) for heads n = lane/4 of the
+    // group, computed once by warp 0 into shared memory.
     const int qn = lane >> 2, qj = lane & 3;
     constexpr int KS = D / 16;
-    uint32_t qhi[KS][2], qlo[KS][2];
-    {
+    if (warp == 0) {
         const bool has = qn < G;
         const int64_t qb = (static_cast<int64_t>(b) * p.Hq + h * G + (has ? qn : 0)) * D;
 #pragma unroll
@@ -430,12 +440,14 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
             int d0, d1;
             if (KBS > 0) { d0 = 16 * ks + 2 * qj; d1 = d0 + 8; }
             else { const int g32 = ks >> 1, half = ks & 1; d0 = 32 * g32 + 8 * qj + 4 * half; d1 = d0 + 2; }
-            float q0 = has ? load_q(p.q, p.q_dtype, qb + d0) : 0.f;
-            float q1 = has ? load_q(p.q, p.q_dtype, qb + d0 + 1) : 0.f;
-            float q2 = has ? load_q(p.q, p.q_dtype, qb + d1) : 0.f;
-            float q3 = has ? load_q(p.q, p.q_dtype, qb + d1 + 1) : 0.f;
-            split_pair(q0, q1, qhi[ks][0], qlo[ks][0]);
-            split_pair(q2, q3, qhi[ks][1], qlo[ks][1]);
+            const float q0 = has ? load_q(p.q, p.q_dtype, qb + d0) : 0.f;
+            const float q1 = has ? load_q(p.q, p.q_dtype, qb + d0 + 1) : 0.f;
+            const float q2 = has ? load_q(p.q, p.q_dtype, qb + d1) : 0.f;
+            const float q3 = has ? load_q(p.q, p.q_dtype, qb + d1 + 1) : 0.f;
+            uint4 f;
+            split_pair(q0, q1, f.x, f.z);
+            split_pair(q2, q3, f.y, f.w);
+            sm.qfrag[ks][lane] = f;
         }
     }
 
@@ -450,10 +462,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
         const uint32_t parity = (c >> 1) & 1;
         const int t0 = t_begin + c * CH;
         const int n = min(CH, t_end - t0);
-        // Direct FP16 K fragments for this warp's 16 tokens, issued before the
-        // wait so the loads overlap it. Permuted dims: lane quad j of row r
+        // Direct FP16 K fragments for this warp's 16 tokens: asynchronous
+        // copies into the warp's staging slots, issued before the wait so
+        // they overlap it and the decode. Permuted dims: lane quad j of row r
         // loads dims [32g + 8j, 32g + 8j + 8) for each 32-dim group g.
-        uint4 kreg[KBS ? 1 : D / 32][2];
         if constexpr (KBS == 0) {
             if (warp < NWM) {
 #pragma unroll
@@ -469,9 +481,12 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
                                                                  static_cast<int64_t>(tt % P) * D * 2);
                     }
 #pragma unroll
-                    for (int g32 = 0; g32 < D / 32; ++g32)
-                        kreg[g32][rr] = row ? __ldg(row + 4 * g32 + qj) : make_uint4(0, 0, 0, 0);
+                    for (int g32 = 0; g32 < D / 32; ++g32) {
+                        if (row) cp_async16(&sm.kstage[warp][rr][g32][lane], row + 4 * g32 + qj);
+                        else sm.kstage[warp][rr][g32][lane] = make_uint4(0, 0, 0, 0);
+                    }
                 }
+                cp_async_commit();
             }
         }
         const bool waited = mbar_wait(&sm.bar[s], parity);
@@ -515,28 +530,36 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 2) attn_fast_ker
         }
         // Tensor-core phase: warp w owns chunk tokens [16w, 16w + 16).
         if (warp < NWM) {
-            float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (KBS == 0) cp_async_wait_all();
+            __syncwarp();
+            // Two independent accumulator chains (even / odd k-steps).
+            float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks) {
+                const uint4 qf = sm.qfrag[ks][lane];
+                float* acc = sa[ks & 1];
                 uint32_t a[4];
                 if constexpr (KBS > 0) {
                     const int mi = lane >> 3, rr = lane & 7;
                     const int row = 16 * warp + rr + ((mi & 1) ? 8 : 0);
                     const int col = 16 * ks + ((mi & 2) ? 8 : 0);
                     ldsm_x4(a, &sm.khi[row][col]);
-                    mma16816(sacc, a[0], a[1], a[2], a[3], qhi[ks][0], qhi[ks][1]);
-                    mma16816(sacc, a[0], a[1], a[2], a[3], qlo[ks][0], qlo[ks][1]);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
                     ldsm_x4(a, &sm.klo[row][col]);
-                    mma16816(sacc, a[0], a[1], a[2], a[3], qhi[ks][0], qhi[ks][1]);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
                 } else {
-                    const uint4& r0 = kreg[ks >> 1][0];
-                    const uint4& r1 = kreg[ks >> 1][1];
+                    const uint4 r0 = sm.kstage[warp][0][ks >> 1][lane];
+                    const uint4 r1 = sm.kstage[warp][1][ks >> 1][lane];
                     if ((ks & 1) == 0) { a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y; }
                     else { a[0] = r0.z; a[2] = r0.w; a[1] = r1.z; a[3] = r1.w; }
-                    mma16816(sacc, a[0], a[1], a[2], a[3], qhi[ks][0], qhi[ks][1]);
-                    mma16816(sacc, a[0], a[1], a[2], a[3], qlo[ks][0], qlo[ks][1]);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
                 }
             }
+            float sacc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sacc[i] = sa[0][i] + sa[1][i];
             // sacc: S^T[tok = qn (+8)][head = 2qj (+1)], in log2 units after scaling.
             const bool v0 = 16 * warp + qn < n, v1 = 16 * warp + qn + 8 < n;
             float sv[4];

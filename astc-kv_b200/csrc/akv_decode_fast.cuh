@@ -51,6 +51,99 @@ __device__ __forceinline__ uint32_t table_entry(float u, bool affine, float sc, 
     return static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
 }
 
+// Weight unquantisation (spec formula) evaluated at compile time for a
+// compile-time weight range, so value tables need no table loads.
+constexpr int cx_replicate(int v, int n, int width) {
+    int out = 0, filled = 0;
+    while (filled < width) {
+        const int k = n < width - filled ? n : width - filled;
+        out = (out << k) | (v >> (n - k));
+        filled += k;
+    }
+    return out;
+}
+
+constexpr int cx_weight(int q, int code) {
+    const int lv[12] = {2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32};
+    const int L = lv[q];
+    const bool tr = L % 3 == 0, qu = L % 5 == 0;
+    const int base = tr ? L / 3 : (qu ? L / 5 : L);
+    int b = 0;
+    while ((1 << b) < base) ++b;
+    int r = 0;
+    if (!tr && !qu) {
+        r = cx_replicate(code, b, 6);
+    } else if (b == 0) {
+        r = tr ? (code == 0 ? 0 : code == 1 ? 32 : 63) : (code * 16 - (code >= 3 ? 1 : 0));
+    } else {
+        const int digit = code >> b, m = code & ((1 << b) - 1);
+        const int a = m & 1, bb = (m >> 1) & 1, c = (m >> 2) & 1;
+        int B = 0, C = 0;
+        if (L == 6) C = 50;
+        else if (L == 10) C = 28;
+        else if (L == 12) { C = 23; B = bb * 0x45; }
+        else if (L == 20) { C = 13; B = bb * 0x42; }
+        else if (L == 24) { C = 11; B = c * 0x42 + bb * 0x21; }
+        const int A = a ? 0x7F : 0;
+        const int T = (digit * C + B) ^ A;
+        r = (A & 0x20) | (T >> 2);
+    }
+    return r > 32 ? r + 1 : r;
+}
+
+// Up to eight colour integers of range `cq` from a colour stream that starts
+// at bit 0 of (clo, chi) and is masked to its length, unquantised to 0..255
+// into registers (no local-memory arrays).
+__device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int (&v)[8]) {
+    const Tables& T = g_akv_tables;
+    const uint32_t shp = __ldg(&T.shape[cq]);
+    const int b = shp & 15;
+    const uint64_t mm = (1ull << b) - 1ull;
+    const uint8_t* un = T.cunq[cq];
+    if (shp & 0x10) {
+        const int gb = 5 * b + 8;
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+            const uint64_t w = window_u128(clo, chi, g * gb);
+            const uint32_t t = static_cast<uint32_t>((w >> b) & 3u) | static_cast<uint32_t>(((w >> (2 * b + 2)) & 3u) << 2) |
+                               static_cast<uint32_t>(((w >> (3 * b + 4)) & 1u) << 4) |
+                               static_cast<uint32_t>(((w >> (4 * b + 5)) & 3u) << 5) |
+                               static_cast<uint32_t>(((w >> (5 * b + 7)) & 1u) << 7);
+            const uint32_t dg = __ldg(&T.trit[t]);
+            const int off[5] = {0, 2, 4, 5, 7};
+#pragma unroll
+            for (int j = 0; j < 5; ++j) {
+                const int i = 5 * g + j;
+                if (i < 8) {
+                    const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
+                    v[i] = __ldg(un + ((((dg >> (2 * j)) & 3u) << b) | m));
+                }
+            }
+        }
+    } else if (shp & 0x20) {
+        const int gb = 3 * b + 7;
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+            const uint64_t w = window_u128(clo, chi, g * gb);
+            const uint32_t qv = static_cast<uint32_t>((w >> b) & 7u) | static_cast<uint32_t>(((w >> (2 * b + 3)) & 3u) << 3) |
+                                static_cast<uint32_t>(((w >> (3 * b + 5)) & 3u) << 5);
+            const uint32_t dg = __ldg(&T.quint[qv]);
+            const int off[3] = {0, 3, 5};
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                const int i = 3 * g + j;
+                if (i < 8) {
+                    const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
+                    v[i] = __ldg(un + ((((dg >> (3 * j)) & 7u) << b) | m));
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __ldg(un + static_cast<uint32_t>(window_u128(clo, chi, i * b) & mm));
+    }
+}
+
 // Fast-class block: header, endpoints, value table and per-texel indices.
 // WQ is the block's weight range (compile time: every BISE position below is
 // a constant).
@@ -101,36 +194,50 @@ __device__ __forceinline__ void decode_fast(uint4 blk, bool affine, float sc, fl
         for (int t = 0; t < N; t += 4) *reinterpret_cast<uint32_t*>(idx + t) = 0u;
     };
     if (cq == 0xFF) { error_block(); return; }
-    int vals[18];
-    {
-        uint64_t clo = window_u128(lo, hi, cstart);
-        uint64_t chi = hi >> cstart;
-        mask_u128(clo, chi, bise_stream_bits_dev(2 * npairs, cq));
-        bise_stream(clo, chi, 2 * npairs, cq, [&](int i, int code) { vals[i] = __ldg(&T.cunq[cq][code]); });
-    }
     int e0[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
-    {
+    uint64_t clo = window_u128(lo, hi, cstart);
+    uint64_t chi = hi >> cstart;
+    mask_u128(clo, chi, bise_stream_bits_dev(2 * npairs, cq));
+    const bool lum_direct = parts == 1 ? cem[0] == 0 : (cem[0] | cem[1] | (parts > 2 ? cem[2] : 0) | (parts > 3 ? cem[3] : 0)) == 0;
+    if (lum_direct) {
+        // Luminance direct (mode 0) on every partition: e0 = v[2q], e1 = v[2q+1].
+        int v[8];
+        colors8(clo, chi, cq, v);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { e0[q] = v[2 * q]; e1[q] = v[2 * q + 1]; }
+    } else {
+        int vals[18];
+        bise_stream(clo, chi, 2 * npairs, cq, [&](int i, int code) { vals[i] = __ldg(&T.cunq[cq][code]); });
         int k = 0;
 #pragma unroll 1
         for (int q = 0; q < parts; ++q) {
             int a[4], bb[4];
             if (!endpoints(cem[q], vals + k, a, bb)) { error_block(); return; }
-            e0[q] = a[0];
-            e1[q] = bb[0];
             k += 2 * ((cem[q] >> 2) + 1);
+            if (q == 0) { e0[0] = a[0]; e1[0] = bb[0]; }
+            else if (q == 1) { e0[1] = a[0]; e1[1] = bb[0]; }
+            else if (q == 2) { e0[2] = a[0]; e1[2] = bb[0]; }
+            else { e0[3] = a[0]; e1[3] = bb[0]; }
         }
     }
     // Direct mode: a table would be larger than the block, so each texel's
     // value is computed in place (identity indices).
     const bool direct = parts * L > N;
-    // Value table: entry q*L + code.
-#pragma unroll 1
-    for (int q = 0; q < (direct ? 0 : parts); ++q) {
+    // Value table: entry q*L + code (weights are compile-time constants).
+    if (!direct) {
 #pragma unroll
-        for (int code = 0; code < L; ++code) {
-            const int w = __ldg(&T.wunq[WQ][code]);
-            const int X = e0[q] * (64 - w) + e1[q] * w;
-            tab[q * L + code] = table_entry(c16_to_unit(static_cast<uint32_t>(4 * X + ((X + 32) >> 6))), affine, sc, of);
+        for (int q = 0; q < 4; ++q) {
+            if (q < parts) {
+#pragma unroll
+                for (int code = 0; code < L; ++code) {
+                    constexpr int dummy = 0;
+                    (void)dummy;
+                    const int w = cx_weight(WQ, code);
+                    const int X = e0[q] * (64 - w) + e1[q] * w;
+                    tab[q * L + code] =
+                        table_entry(c16_to_unit(static_cast<uint32_t>(4 * X + ((X + 32) >> 6))), affine, sc, of);
+                }
+            }
         }
     }
     // Weight stream (bit-reversed, masked) and partition pattern.
@@ -151,7 +258,7 @@ __device__ __forceinline__ void decode_fast(uint4 blk, bool affine, float sc, fl
         if (direct) {
             const int a = part == 0 ? e0[0] : part == 1 ? e0[1] : part == 2 ? e0[2] : e0[3];
             const int bq = part == 0 ? e1[0] : part == 1 ? e1[1] : part == 2 ? e1[2] : e1[3];
-            const int w = __ldg(&T.wunq[WQ][code]);
+            const int w = __ldg(&T.wunq[WQ][code]);  // code is a runtime value here
             const int X = a * (64 - w) + bq * w;
             tab[i] = table_entry(c16_to_unit(static_cast<uint32_t>(4 * X + ((X + 32) >> 6))), affine, sc, of);
             code = i;
