@@ -18,6 +18,8 @@ AKV_LAYOUT_SCALAR, AKV_LAYOUT_RGBA = 0, 1
 AKV_NORM_PAGE_CHANNEL, AKV_NORM_TOKEN, AKV_NORM_BLOCK_AFFINE = 0, 1, 2
 AKV_Q_F32, AKV_Q_BF16, AKV_Q_F16 = 0, 1, 2
 AKV_PHASE_SPLIT, AKV_PHASE_MERGE = 1, 2
+AKV_ERR_STATIC_WORKSPACE = 8
+AKV_STATIC_WORKSPACE_BYTES = 8 << 20
 
 LAYOUTS = {"scalar": AKV_LAYOUT_SCALAR, "rgba": AKV_LAYOUT_RGBA}
 NORMS = {"page_channel": AKV_NORM_PAGE_CHANNEL, "token": AKV_NORM_TOKEN, "block_affine": AKV_NORM_BLOCK_AFFINE}
@@ -52,7 +54,7 @@ class AkvAttnDesc(ct.Structure):
 EXPORTS = (
     "akv_cuda_error", "akv_cuda_abi_version", "akv_cuda_init", "akv_cuda_decode_blocks", "akv_cuda_decode_image",
     "akv_cuda_attention_workspace", "akv_cuda_decode_attention", "akv_cuda_decode_attention_phase",
-    "akv_cuda_restore_plane", "akv_cuda_struct_size",
+    "akv_cuda_decode_attention_noalloc", "akv_cuda_restore_plane", "akv_cuda_struct_size",
     "akv_cuda_host_tables", "akv_host_encode", "akv_host_random_blocks",
 )
 
@@ -91,6 +93,7 @@ def lib() -> ct.CDLL:
         l.akv_cuda_attention_workspace.restype = sz
         l.akv_cuda_decode_attention.argtypes = [ct.POINTER(AkvAttnDesc), vp]
         l.akv_cuda_decode_attention_phase.argtypes = [ct.POINTER(AkvAttnDesc), ct.c_int, vp]
+        l.akv_cuda_decode_attention_noalloc.argtypes = [ct.POINTER(AkvAttnDesc), vp]
         l.akv_cuda_restore_plane.argtypes = [ct.POINTER(AkvPlane), i32, i32, i32, i32, i32, vp, i32, i32, vp, vp, vp]
         l.akv_cuda_struct_size.argtypes = [ct.c_int]
         l.akv_cuda_struct_size.restype = sz
@@ -102,7 +105,8 @@ def lib() -> ct.CDLL:
             f = getattr(l, name)
             if f.restype is ct.c_int or name in ("akv_cuda_init", "akv_cuda_decode_blocks", "akv_cuda_decode_image",
                                                   "akv_cuda_decode_attention", "akv_cuda_restore_plane",
-                                                  "akv_cuda_decode_attention_phase", "akv_host_encode", "akv_host_random_blocks"):
+                                                  "akv_cuda_decode_attention_phase", "akv_cuda_decode_attention_noalloc",
+                                                  "akv_host_encode", "akv_host_random_blocks"):
                 f.restype = ct.c_int
         if l.akv_cuda_struct_size(0) != ct.sizeof(AkvPlane) or l.akv_cuda_struct_size(1) != ct.sizeof(AkvAttnDesc):
             raise RuntimeError("libakv_cuda.so struct layout does not match this binding")

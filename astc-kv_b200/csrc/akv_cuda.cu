@@ -19,6 +19,11 @@
 namespace akv {
 namespace {
 
+// Split scratch of akv_cuda_decode_attention_noalloc: static device memory,
+// one copy per device that loads the library. Host code sees only a stand-in
+// for this symbol; the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) float g_static_workspace[AKV_STATIC_WORKSPACE_BYTES / sizeof(float)];
+
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
 bool g_init_done[kMaxDevices];
@@ -58,6 +63,27 @@ int ensure_init() {
     if (cudaStreamIsCapturing(cudaStreamLegacy, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
         return AKV_ERR_NOT_INITIALIZED;
     return init_device(dev);
+}
+
+std::mutex g_static_mu;
+void* g_static_ptr[kMaxDevices];
+
+// Device address of g_static_workspace on the current device (looked up once
+// per device, with that device current).
+int static_workspace(void** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AKV_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_static_workspace) != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            return AKV_ERR_CUDA;
+        }
+        g_static_ptr[dev] = ptr;
+    }
+    *out = g_static_ptr[dev];
+    return AKV_OK;
 }
 
 int sm_count() {
@@ -341,6 +367,8 @@ const char* akv_cuda_error(int code) {
         case AKV_ERR_BAD_BLOCK_TABLE: return "block table entry outside [0, num_pages)";
         case AKV_ERR_WORKSPACE: return "workspace missing or smaller than akv_cuda_attention_workspace()";
         case AKV_ERR_TIMEOUT: return "a kernel's bounded wait for its own asynchronous copies ran out";
+        case AKV_ERR_STATIC_WORKSPACE:
+            return "the call needs more split scratch than the library's static workspace (AKV_STATIC_WORKSPACE_BYTES)";
         default: return "unknown status code";
     }
 }
@@ -434,6 +462,19 @@ int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* strea
     }
     const Variant* v = find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl);
     return v->fn(p, static_cast<cudaStream_t>(stream), phase);
+}
+
+int akv_cuda_decode_attention_noalloc(const AkvAttnDesc* d, void* stream) {
+    AttnPlan plan;
+    if (int st = plan_attention(d, &plan)) return st;
+    if (plan.ws > static_cast<size_t>(AKV_STATIC_WORKSPACE_BYTES)) return AKV_ERR_STATIC_WORKSPACE;
+    if (int st = ensure_init()) return st;
+    void* ws = nullptr;
+    if (int st = static_workspace(&ws)) return st;
+    AkvAttnDesc local = *d;
+    local.workspace_dev = ws;
+    local.workspace_bytes = AKV_STATIC_WORKSPACE_BYTES;
+    return akv_cuda_decode_attention(&local, stream);
 }
 
 int akv_cuda_restore_plane(const AkvPlane* plane, int32_t batch, int32_t kv_heads, int32_t max_tokens, int32_t head_dim,

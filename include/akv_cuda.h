@@ -32,6 +32,7 @@ extern "C" {
 #define AKV_ERR_BAD_BLOCK_TABLE 5    /* a kernel saw a block-table entry outside [0, num_pages) */
 #define AKV_ERR_WORKSPACE 6          /* workspace missing or smaller than akv_cuda_attention_workspace() */
 #define AKV_ERR_TIMEOUT 7            /* a kernel's bounded wait for its own async copies ran out */
+#define AKV_ERR_STATIC_WORKSPACE 8   /* the call needs more split scratch than AKV_STATIC_WORKSPACE_BYTES */
 
 /* Decoder output views of the 16-bit interpolation result C of each texel. */
 #define AKV_OUT_UNORM8 0   /* C >> 8 (decode_unorm8), 4 bytes per texel */
@@ -158,6 +159,34 @@ int akv_cuda_decode_attention(const AkvAttnDesc* desc, void* stream);
 #define AKV_PHASE_SPLIT 1
 #define AKV_PHASE_MERGE 2
 int akv_cuda_decode_attention_phase(const AkvAttnDesc* desc, int phase, void* stream);
+
+/*
+ * Decode attention for callers that cannot allocate device memory.
+ * No counterpart in the reference: it is an addition of this library.
+ *
+ * Some callers of this code cannot call cudaMalloc or hand out a workspace:
+ * bindings from other language runtimes (cgo, JNI, N-API) that reach the GPU
+ * only through this C ABI and own no device allocator; hosts whose memory
+ * belongs to a framework's caching allocator, where a stray cudaMalloc
+ * fragments the pool or stalls every stream; serving loops with a fixed
+ * device-memory budget. This entry point takes the same descriptor as
+ * akv_cuda_decode_attention, ignores workspace_dev / workspace_bytes, and
+ * keeps the split partials in a static device array of
+ * AKV_STATIC_WORKSPACE_BYTES compiled into the library (every GPU that loads
+ * the library holds that array until the process exits). It allocates
+ * nothing.
+ *   - A descriptor that needs more scratch than that (see
+ *     akv_cuda_attention_workspace) returns AKV_ERR_STATIC_WORKSPACE.
+ *   - The first call on a device looks up the array's device address (and
+ *     fills the decode tables if akv_cuda_init has not run there); make that
+ *     first call, or akv_cuda_init plus one call, before any stream capture.
+ *   - All calls share the one array and it keeps the last call's contents;
+ *     nothing in it needs to start at zero (every partial a call reads, that
+ *     call wrote first). Calls whose kernels overlap on the GPU (different
+ *     streams, or several host threads) race on the array: serialise them.
+ */
+#define AKV_STATIC_WORKSPACE_BYTES (8u << 20)
+int akv_cuda_decode_attention_noalloc(const AkvAttnDesc* desc, void* stream);
 
 /*
  * Restore a whole plane to fp32 [batch][kv_heads][max_tokens][head_dim]:
