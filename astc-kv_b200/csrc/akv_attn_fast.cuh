@@ -140,150 +140,188 @@ __device__ __forceinline__ int64_t meta_chunk_offset(int norm, int cols, int t_i
                                          : (norm == AKV_NORM_TOKEN ? t_in_page : 0);
 }
 
-// Scratch of the sorted decode for one plane-chunk of up to NB blocks.
-template <int NB, int TEX>
+// Scratch of the decode of one plane-chunk of up to NB blocks by NT threads.
+template <int NB, int NT>
 struct DecodeScratch {
-    uint32_t tab[NB][TEX];
-    uint32_t idx[NB][(TEX + 3) / 4];
-    uint16_t order[NB];
-    uint8_t cls[NB];
-    int count[kNumCls];
-    int base[kNumCls];
-    int nslow;
+    static constexpr int kSlowCap = NB < 64 ? NB : 64;
+    int count[kNumKeys];        // first: the same counters for every plane sharing the scratch
+    uint32_t tab[kTabCap][NT];  // value tables, thread-interleaved (conflict-free lookups)
+    uint16_t order[NB];         // block indices in key order
+    uint8_t key[NB];
+    uint16_t slow_blk[kSlowCap];
+    BlockDesc<1> desc[kSlowCap];
+    uint8_t w[kSlowCap][64];
 };
 
-// Per-texel scratch of slow blocks (aliases the tiles, which are free while
-// a chunk is being decoded).
-template <int NB>
-struct SlowScratch {
-    static constexpr int kCap = NB < 96 ? NB : 96;  // fits in the two tiles of every variant
-    BlockDesc<1> desc[kCap];
-    uint8_t w[kCap][64];
-};
+// Texels of one table-decoded block -> the hi/lo tiles (pairs of columns per
+// 32-bit store). Rows at or past `rows` are written as zeros.
+template <int BS, int LD>
+__device__ __forceinline__ void write_block(const Idx<BS>& ix, const uint32_t* tab, int nt, int norm,
+                                            const __half* moff, const __half* mscl, int row0, int col0, int rows,
+                                            int cols, __half (*thi)[LD], __half (*tlo)[LD]) {
+    const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
+#pragma unroll
+    for (int y = 0; y < BS; ++y) {
+        const bool rok = y < rows;
+        float rs = 0.f, ro = 0.f;
+        if (norm == AKV_NORM_TOKEN && rok) {
+            rs = __half2float(mscl[row0 + y]);
+            ro = __half2float(moff[row0 + y]);
+        }
+#pragma unroll
+        for (int x = 0; x < BS; x += 2) {
+            if (x < cols) {
+                const int i = y * BS + x;
+                const uint32_t i0 = (ix.w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+                const uint32_t i1 = (ix.w[(i + 1) >> 2] >> (8 * ((i + 1) & 3))) & 0xFFu;
+                const uint32_t a = tab[i0 * nt], b2 = tab[i1 * nt];
+                uint32_t h, l;
+                if (affine) {
+                    h = __byte_perm(a, b2, 0x5410);
+                    l = __byte_perm(a, b2, 0x7632);
+                } else {
+                    float s0 = rs, o0 = ro, s1 = rs, o1 = ro;
+                    if (norm == AKV_NORM_PAGE_CHANNEL) {
+                        s0 = __half2float(mscl[col0 + x]); o0 = __half2float(moff[col0 + x]);
+                        s1 = __half2float(mscl[col0 + x + 1]); o1 = __half2float(moff[col0 + x + 1]);
+                    }
+                    split_pair(fmaf(__uint_as_float(a), s0, o0), fmaf(__uint_as_float(b2), s1, o1), h, l);
+                }
+                if (!rok) { h = 0u; l = 0u; }
+                *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
+                *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
+            }
+        }
+    }
+}
+
+// One texel value v (fp32) -> the hi/lo tiles.
+template <int LD>
+__device__ __forceinline__ void put_texel(float v, bool ok, int row, int col, __half (*thi)[LD], __half (*tlo)[LD]) {
+    const __half hv = __float2half_rn(v);
+    thi[row][col] = ok ? hv : __float2half_rn(0.f);
+    tlo[row][col] = ok ? __float2half_rn(v - __half2float(hv)) : __float2half_rn(0.f);
+}
 
 // Decode one plane's chunk into the hi/lo tiles. All threads call it.
+//   phase 0  key per block (fast weight range / constant / slow), ranks by
+//            warp-aggregated shared-memory atomics, scatter into key order;
+//   phase 1  thread per block in key order (lanes of a warp mostly share a
+//            code path): fast and constant blocks go straight to the tiles,
+//            slow blocks get their descriptor decoded;
+//   phase 1b thread per texel of the slow blocks.
 template <int BS, int D, int THREADS, int NB, int LD>
-__device__ __forceinline__ void decode_plane_sorted(const uint4* raw, const __half* moff, const __half* mscl, int norm,
-                                                    int cols, int rows_blk, int n, bool valid,
-                                                    DecodeScratch<NB, BS * BS>& ds, SlowScratch<NB>& ss,
-                                                    __half (*thi)[LD], __half (*tlo)[LD]) {
+__device__ __forceinline__ void decode_plane(const uint4* raw, const __half* moff, const __half* mscl, int norm,
+                                             int cols, int rows_blk, int n, bool valid,
+                                             DecodeScratch<NB, THREADS>& ds, __half (*thi)[LD], __half (*tlo)[LD]) {
     constexpr int N = BS * BS;
     constexpr int fp = footprint_index(BS);
+    constexpr int PER = (NB + THREADS - 1) / THREADS;
+    constexpr int kCap = DecodeScratch<NB, THREADS>::kSlowCap;
     const int nblk = rows_blk * cols;
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
-    // Phase 0: classify and count.
-    if (threadIdx.x < kNumCls) ds.count[threadIdx.x] = 0;
-    __syncthreads();
-    for (int i = threadIdx.x; i < nblk; i += THREADS) {
-        const int c = classify<BS>(raw[i]);
-        ds.cls[i] = static_cast<uint8_t>(c);
-        atomicAdd(&ds.count[c], 1);
+    const int tid = threadIdx.x, lane = tid & 31;
+    // Phase 0: keys and ranks.
+    int rank[PER];
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+        const int i = tid + r * THREADS;
+        rank[r] = -1;
+        if (i < nblk) {
+            const int k = block_key<BS>(raw[i]);
+            ds.key[i] = static_cast<uint8_t>(k);
+            const unsigned peers = __match_any_sync(__activemask(), k);
+            const int leader = __ffs(peers) - 1;
+            int base = 0;
+            if (lane == leader) base = atomicAdd(&ds.count[k], __popc(peers));
+            base = __shfl_sync(peers, base, leader);
+            rank[r] = base + __popc(peers & ((1u << lane) - 1u));
+        }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int c = 0; c < kNumCls; ++c) { ds.base[c] = acc; acc += ds.count[c]; }
-        ds.nslow = ds.count[kClsSlow];
+    const int s0 = ds.count[kKeyConst];     // slow blocks sit at order[s0, s0 + nslow)
+    const int nslow = ds.count[kKeySlow];
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+        if (rank[r] >= 0) {
+            const int i = tid + r * THREADS;
+            const int k = ds.key[i];
+            int base = 0;
+            for (int j = 0; j < k; ++j) base += ds.count[j];
+            ds.order[base + rank[r]] = static_cast<uint16_t>(i);
+        }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < nblk; i += THREADS) {
-        const int c = ds.cls[i];
-        ds.order[atomicAdd(&ds.base[c], 1)] = static_cast<uint16_t>(i);
-    }
-    __syncthreads();
-    // Phase 1: class-ordered block decode.
-    const int s0 = ds.base[kClsSlow] - ds.count[kClsSlow];  // first slow block in `order`
-    for (int k = threadIdx.x; k < nblk; k += THREADS) {
+    if (tid < kNumKeys) ds.count[tid] = 0;  // for the next plane-chunk (read after two more barriers)
+    // Phase 1.
+    for (int k = tid; k < nblk; k += THREADS) {
         const int i = ds.order[k];
-        const int c = ds.cls[i];
+        const int key = ds.key[i];
         const uint4 blk = raw[i];
+        const int br = i / cols, bc = i - br * cols;
+        const int row0 = br * BS, col0 = bc * BS;
+        const int rows = valid ? min(BS, n - row0) : 0;
+        const int ncol = min(BS, D - col0);
         const float sc = affine ? __half2float(mscl[i]) : 0.f;
         const float of = affine ? __half2float(moff[i]) : 0.f;
-        uint32_t* tab = ds.tab[i];
-        if (c >= kClsFast) {
-            decode_fast_any<BS>(c - kClsFast, blk, affine, sc, of, tab, reinterpret_cast<uint8_t*>(ds.idx[i]));
+        uint32_t* tab = &ds.tab[0][tid];
+        if (key != kKeySlow) {
+            Idx<BS> ix;
+            if (key >= kKeyFast) {
+                decode_fast_any<BS>(key - kKeyFast, blk, affine, sc, of, tab, THREADS, ix);
+            } else {
+                tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+#pragma unroll
+                for (int j = 0; j < Idx<BS>::NW; ++j) ix.w[j] = 0u;
+            }
+            write_block<BS, LD>(ix, tab, THREADS, norm, moff, mscl, row0, col0, rows, ncol, thi, tlo);
             continue;
         }
         const int slot = k - s0;
-        const bool scratch = c == kClsSlow && slot < SlowScratch<NB>::kCap;
-        BlockDesc<1> dl;
-        uint8_t wl[64];
-        BlockDesc<1>& d = scratch ? ss.desc[slot] : dl;
-        uint8_t* w = scratch ? ss.w[slot] : wl;
-        decode_header<1>(blk, fp, d, w);
-        if (c == kClsConst || (d.info & ((1u << kInfoVoid) | (1u << kInfoError)))) {
-            uint32_t cv[1];
-            texel_values<BS, 1>(d, w, 0, 0, cv);
-            tab[0] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
-#pragma unroll
-            for (int t = 0; t < (N + 3) / 4; ++t) ds.idx[i][t] = 0u;
-            ds.cls[i] = kClsConst;
+        if (slot < kCap) {
+            decode_header<1>(blk, fp, ds.desc[slot], ds.w[slot]);
+            ds.slow_blk[slot] = static_cast<uint16_t>(i);
             continue;
         }
-#pragma unroll
-        for (int t = 0; t < N; t += 4) ds.idx[i][t / 4] = t | ((t + 1) << 8) | ((t + 2) << 16) | ((t + 3) << 24);
-        if (!scratch) {
-            // Beyond the scratch capacity: evaluate the texels here.
+        // Beyond the scratch capacity: evaluate the texels here.
+        BlockDesc<1> d;
+        uint8_t wl[64];
+        decode_header<1>(blk, fp, d, wl);
 #pragma unroll 1
-            for (int t = 0; t < N; ++t) {
-                uint32_t cv[1];
-                texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
-                tab[t] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
-            }
+        for (int t = 0; t < N; ++t) {
+            const int x = t % BS, y = t / BS;
+            if (x >= ncol) continue;
+            uint32_t cv[1];
+            texel_values<BS, 1>(d, wl, x, y, cv);
+            const float u = c16_to_unit(cv[0]);
+            float s = sc, o = of;
+            if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row0 + y]); o = __half2float(moff[row0 + y]); }
+            if (norm == AKV_NORM_PAGE_CHANNEL) { s = __half2float(mscl[col0 + x]); o = __half2float(moff[col0 + x]); }
+            put_texel<LD>(fmaf(u, s, o), y < rows, row0 + y, col0 + x, thi, tlo);
         }
     }
     __syncthreads();
-    // Phase 1b: texels of slow blocks held in the scratch, thread per texel.
-    const int nscr = min(ds.nslow, SlowScratch<NB>::kCap);
-    if (nscr > 0) {
-        const int ntex = nscr * N;
-        for (int k = threadIdx.x; k < ntex; k += THREADS) {
-            const int slot = k / N;
-            const int i = ds.order[s0 + slot];
-            if (ds.cls[i] != kClsSlow) continue;  // turned out constant
-            const int t = k - slot * N;
+    if (nslow > 0) {
+        // Phase 1b: texels of the slow blocks held in the scratch.
+        const int ntex = min(nslow, kCap) * N;
+        for (int task = tid; task < ntex; task += THREADS) {
+            const int slot = task / N, t = task - slot * N;
+            const int i = ds.slow_blk[slot];
+            const int x = t % BS, y = t / BS;
+            const int br = i / cols, bc = i - br * cols;
+            const int row = br * BS + y, col = bc * BS + x;
+            if (col >= D) continue;
             uint32_t cv[1];
-            texel_values<BS, 1>(ss.desc[slot], ss.w[slot], t % BS, t / BS, cv);
-            const float sc = affine ? __half2float(mscl[i]) : 0.f;
-            const float of = affine ? __half2float(moff[i]) : 0.f;
-            ds.tab[i][t] = table_entry(c16_to_unit(cv[0]), affine, sc, of);
+            texel_values<BS, 1>(ds.desc[slot], ds.w[slot], x, y, cv);
+            const float u = c16_to_unit(cv[0]);
+            float s, o;
+            if (affine) { s = __half2float(mscl[i]); o = __half2float(moff[i]); }
+            else if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row]); o = __half2float(moff[row]); }
+            else { s = __half2float(mscl[col]); o = __half2float(moff[col]); }
+            put_texel<LD>(fmaf(u, s, o), valid && row < n, row, col, thi, tlo);
         }
         __syncthreads();
     }
-    // Phase 2: tiles, thread per (block, texel row).
-    const int ntask = nblk * BS;
-    for (int task = threadIdx.x; task < ntask; task += THREADS) {
-        const int bi = task / BS, y = task - bi * BS;
-        const int br = bi / cols, bc = bi - br * cols;
-        const int row = br * BS + y;
-        const bool ok = valid && row < n;
-        const uint8_t* ix = reinterpret_cast<const uint8_t*>(ds.idx[bi]) + y * BS;
-        const uint32_t* tb = ds.tab[bi];
-        float tsc = 0.f, tof = 0.f;
-        if (norm == AKV_NORM_TOKEN) { tsc = __half2float(mscl[row]); tof = __half2float(moff[row]); }
-#pragma unroll
-        for (int x = 0; x < BS; x += 2) {
-            const int col = bc * BS + x;
-            if (col >= D) break;
-            const uint32_t a = tb[ix[x]], b2 = tb[ix[x + 1]];
-            uint32_t h, l;
-            if (affine) {
-                h = __byte_perm(a, b2, 0x5410);
-                l = __byte_perm(a, b2, 0x7632);
-            } else {
-                float s0 = tsc, o0 = tof, s1 = tsc, o1 = tof;
-                if (norm == AKV_NORM_PAGE_CHANNEL) {
-                    s0 = __half2float(mscl[col]); o0 = __half2float(moff[col]);
-                    s1 = __half2float(mscl[col + 1]); o1 = __half2float(moff[col + 1]);
-                }
-                split_pair(fmaf(__uint_as_float(a), s0, o0), fmaf(__uint_as_float(b2), s1, o1), h, l);
-            }
-            if (!ok) { h = 0u; l = 0u; }
-            *reinterpret_cast<uint32_t*>(&thi[row][col]) = h;
-            *reinterpret_cast<uint32_t*>(&tlo[row][col]) = l;
-        }
-    }
-    __syncthreads();
 }
 
 // ------------------------------------------------------------------ kernel
@@ -304,8 +342,8 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, VBS * VBS>);
-    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), KBS * KBS>) : 0;
+    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS>);
+    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
@@ -328,7 +366,7 @@ struct Smem {
     __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[C::NWM][8][16];
     __align__(16) uint4 qfrag[D / 16][32];                         // per lane: q hi (2 words) | q lo (2 words)
-    __align__(16) uint4 kstage[KBS ? 1 : C::NWM][2][KBS ? 1 : D / 32][32];  // FP16 K fragments per MMA warp
+
     float wm[C::NWM][8];
     float wl[C::NWM][8];
 };
@@ -364,6 +402,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         mbar_init(&sm.bar[1], 1);
         fence_mbar_init();
     }
+    if (tid < kNumKeys) reinterpret_cast<DecodeScratch<C::VBLK, THREADS>*>(sm.ds)->count[tid] = 0;
     __syncthreads();
 
     // Producer: stage `s` <- chunk `c` (one elected thread).
@@ -462,33 +501,6 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         const uint32_t parity = (c >> 1) & 1;
         const int t0 = t_begin + c * CH;
         const int n = min(CH, t_end - t0);
-        // Direct FP16 K fragments for this warp's 16 tokens: asynchronous
-        // copies into the warp's staging slots, issued before the wait so
-        // they overlap it and the decode. Permuted dims: lane quad j of row r
-        // loads dims [32g + 8j, 32g + 8j + 8) for each 32-dim group g.
-        if constexpr (KBS == 0) {
-            if (warp < NWM) {
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const int tr = 16 * warp + qn + 8 * rr;
-                    const int tt = t0 + tr;
-                    const uint4* row = nullptr;
-                    if (tr < n) {
-                        const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
-                        if (phys >= 0)
-                            row = reinterpret_cast<const uint4*>(p.k.data + b * p.k.sB + h * p.k.sH +
-                                                                 static_cast<int64_t>(phys) * p.k.sP +
-                                                                 static_cast<int64_t>(tt % P) * D * 2);
-                    }
-#pragma unroll
-                    for (int g32 = 0; g32 < D / 32; ++g32) {
-                        if (row) cp_async16(&sm.kstage[warp][rr][g32][lane], row + 4 * g32 + qj);
-                        else sm.kstage[warp][rr][g32][lane] = make_uint4(0, 0, 0, 0);
-                    }
-                }
-                cp_async_commit();
-            }
-        }
         const bool waited = mbar_wait(&sm.bar[s], parity);
         if (__syncthreads_or(!waited)) {
             stuck = true;
@@ -496,18 +508,16 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         }
         const bool valid = sm.valid[s] != 0;
         // Decode V (and K) tiles.
-        auto& slow = *reinterpret_cast<SlowScratch<C::VBLK>*>(&sm.vhi[0][0]);
-        decode_plane_sorted<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
-                                                         C::VCOLS, CH / VBS, n, valid,
-                                                         *reinterpret_cast<DecodeScratch<C::VBLK, VBS * VBS>*>(sm.ds),
-                                                         slow, sm.vhi, sm.vlo);
+        decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
+                                                  CH / VBS, n, valid,
+                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS>*>(sm.ds), sm.vhi,
+                                                  sm.vlo);
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
-            auto& kslow = *reinterpret_cast<SlowScratch<KN>*>(&sm.khi[0][0]);
-            decode_plane_sorted<KB, D, THREADS, KN, LD>(
-                sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS, CH / KB, n, valid,
-                *reinterpret_cast<DecodeScratch<KN, KB * KB>*>(sm.ds), kslow, sm.khi, sm.klo);
+            decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
+                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS>*>(sm.ds),
+                                                sm.khi, sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;
             if (sc > 0) {
@@ -523,6 +533,31 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
                 __syncthreads();
             }
         }
+        // Direct FP16 K fragments for this warp's 16 tokens (loaded after the
+        // decode so they do not hold registers through it). Permuted dims:
+        // lane quad j of row r loads dims [32g + 8j, 32g + 8j + 8) for each
+        // 32-dim group g.
+        uint4 kreg[KBS ? 1 : D / 32][2];
+        if constexpr (KBS == 0) {
+            if (warp < NWM) {
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int tr = 16 * warp + qn + 8 * rr;
+                    const int tt = t0 + tr;
+                    const uint4* row = nullptr;
+                    if (tr < n) {
+                        const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
+                        if (phys >= 0)
+                            row = reinterpret_cast<const uint4*>(p.k.data + b * p.k.sB + h * p.k.sH +
+                                                                 static_cast<int64_t>(phys) * p.k.sP +
+                                                                 static_cast<int64_t>(tt % P) * D * 2);
+                    }
+#pragma unroll
+                    for (int g32 = 0; g32 < D / 32; ++g32)
+                        kreg[g32][rr] = row ? __ldg(row + 4 * g32 + qj) : make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
         // The raw stage is consumed: refill it with chunk c + 2.
         if (tid == 0 && c + 2 < nchunks) {
             fence_proxy_async();
@@ -530,7 +565,6 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         }
         // Tensor-core phase: warp w owns chunk tokens [16w, 16w + 16).
         if (warp < NWM) {
-            if constexpr (KBS == 0) cp_async_wait_all();
             __syncwarp();
             // Two independent accumulator chains (even / odd k-steps).
             float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -549,8 +583,8 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
                     ldsm_x4(a, &sm.klo[row][col]);
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
                 } else {
-                    const uint4 r0 = sm.kstage[warp][0][ks >> 1][lane];
-                    const uint4 r1 = sm.kstage[warp][1][ks >> 1][lane];
+                    const uint4 r0 = kreg[ks >> 1][0];
+                    const uint4 r1 = kreg[ks >> 1][1];
                     if ((ks & 1) == 0) { a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y; }
                     else { a[0] = r0.z; a[2] = r0.w; a[1] = r1.z; a[3] = r1.w; }
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);

@@ -16,6 +16,11 @@ Workloads (``--workload``; the default is the benchmark line):
   c3      Llama-3-70B-shaped: ASTC 4x4 K + 2-channel FP16 side plane, ASTC 8x8 V.
   c4      Ragged paged atlas: 64 sequences of U[1024, 65536] tokens, 256-token
           pages of a shared 4x4 V atlas, permuted pages, int32 block table.
+  decode4 / decode6 / decode8
+          The config-4 standalone decode microbench: 1 GiB of random legal
+          ASTC blocks of one footprint (every block mode, 1-4 partitions,
+          dual plane, void extent) decoded to UNORM8 RGBA; the CPU baseline
+          decodes a sample of the same blocks with the C oracle on all cores.
 A step is one decode-attention pass over every sequence of the batch.
 
 Multi-GPU: one process per GPU (torchrun). Sequences are independent, so each
@@ -158,6 +163,93 @@ def encoder_pool(block: int, layout: str, D: int, rows: int, seed: int, norm: st
         P += block
     e = A.encode_tensor(x, {"block": block, "layout": layout, "normalization": norm}, page_tokens=P, quality=60)
     return e.blocks_array()[0]
+
+
+class DecodeWorkload:
+    """Config-4 decode microbench: 1 GiB of random legal blocks -> UNORM8."""
+
+    def __init__(self, name: str, rank: int, device, blocks_total: int = 1 << 26):
+        import torch
+        import astc_kv_cuda as A
+        self.name = name
+        self.block = int(name[-1])
+        # A pool of distinct random legal blocks, tiled to 1 GiB on the device.
+        pool = torch.from_numpy(A.random_blocks(1 << 20, self.block, seed=20261029 + rank)).to(device)
+        reps = blocks_total // pool.shape[0]
+        self.blocks = pool.repeat(reps, 1).contiguous()
+        self.n = self.blocks.shape[0]
+        tex = self.block * self.block
+        self.out = torch.empty(self.n, self.block, self.block, 4, dtype=torch.uint8, device=device)
+        self.bytes = self.n * 16 + self.n * tex * 4
+        self.tokens = self.n  # units: blocks
+        self.sample = pool[:1 << 16].cpu().numpy()
+        self.desc = {"workload": f"config4_decode_microbench_{self.block}x{self.block}", "blocks": self.n,
+                     "block_bytes": self.n * 16, "output": "UNORM8 RGBA", "output_bytes": self.n * tex * 4,
+                     "blocks_source": "random legal LDR blocks (1 Mi distinct, tiled)"}
+
+    def run(self):
+        from astc_kv_cuda.ops import decode_blocks
+        decode_blocks(self.blocks, self.block, "unorm8", out=self.out)
+
+
+def run_decode(args) -> dict | None:
+    import torch
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    import astc_kv_cuda as A
+    A.init(local)
+    wl = DecodeWorkload(args.workload, rank, dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wl.run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clk:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            wl.run()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = ev[0].elapsed_time(ev[-1])
+    (total_ms,) = reduce_max([total_ms], world, dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    hbm, src = peaks()
+    per = total_ms / args.steps
+    achieved = wl.bytes / (per * 1e-3) / 1e9
+    line = {"metric": METRIC + " [decode microbench: blocks/s]", "value": wl.n * world * args.steps / (total_ms * 1e-3),
+            "unit": "blocks/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic random legal blocks", "config": {**wl.desc, "l2": "inputs larger than L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                         "peak_source": src, "kernel": "decode_blocks_kernel", "kernel_ms": per,
+                         "traffic": None, "bytes": "16 B read + texels*4 B written per block"},
+            "clocks": clk.summary(), "gpu_launches": args.steps}
+    if world == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, str(ROOT))
+        from oracle import oracle as O
+        threads = O.cpu_threads()
+        O.decode_blocks(wl.sample[:1024], wl.block, O.OUT_UNORM8, threads=threads)
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds:
+            O.decode_blocks(wl.sample, wl.block, O.OUT_UNORM8, threads=threads)
+            done += wl.sample.shape[0]
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": done / dt, "unit": "blocks/s", "cores": threads, "kind": "port",
+                                "sample": f"{done} random legal blocks decoded to UNORM8 by the C oracle on {threads} threads"}
+    return line
 
 
 class Workload:
@@ -494,14 +586,19 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c2")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "decode4", "decode6", "decode8"], default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling of small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if args.impl == "reference":
+        line = run_reference(args)
+    elif args.workload.startswith("decode"):
+        line = run_decode(args)
+    else:
+        line = run_ours(args)
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -60,25 +60,38 @@ extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, u
 
 extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 
-// The fast per-block path of the sorted decode: class, then (for fast
-// classes) table + indices; returns the fp16-view values of the R channel
-// per texel, or -1 in cls for blocks that take the per-texel path.
+// The fast per-block path of the attention kernel's plane decode: sort key,
+// then (fast keys) value table + per-texel index bytes, or (constant keys)
+// the block's single value. Returns the fp16-view values of the R channel
+// per texel, or -1 for blocks that take the per-texel path; `cls` gets the key.
 extern "C" int emu_decode_fast_r(const uint8_t* blocks, int64_t n, int bs, float* out, int* cls) {
     static bool ready = false;
     if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
+    namespace F = akv::fast;
     for (int64_t i = 0; i < n; ++i) {
         uint4 b;
         std::memcpy(&b, blocks + 16 * i, 16);
-        int c = bs == 4 ? akv::fast::classify<4>(b) : bs == 6 ? akv::fast::classify<6>(b) : akv::fast::classify<8>(b);
+        const int c = bs == 4 ? F::block_key<4>(b) : bs == 6 ? F::block_key<6>(b) : F::block_key<8>(b);
         cls[i] = c;
         const int N = bs * bs;
-        if (c < akv::fast::kClsFast) { for (int t = 0; t < N; ++t) out[i * N + t] = -1.f; continue; }
-        uint32_t tab[64];
-        uint8_t idx[64];
-        if (bs == 4) akv::fast::decode_fast_any<4>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
-        else if (bs == 6) akv::fast::decode_fast_any<6>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
-        else akv::fast::decode_fast_any<8>(c - akv::fast::kClsFast, b, false, 0.f, 0.f, tab, idx);
-        for (int t = 0; t < N; ++t) out[i * N + t] = __uint_as_float(tab[idx[t]]);
+        if (c == F::kKeySlow) { for (int t = 0; t < N; ++t) out[i * N + t] = -1.f; continue; }
+        if (c == F::kKeyConst) {
+            const float u = akv::c16_to_unit(F::const_c16(b));
+            for (int t = 0; t < N; ++t) out[i * N + t] = u;
+            continue;
+        }
+        uint32_t tab[F::kTabCap];
+        uint32_t words[16];
+        int L = 0;
+        if (bs == 4) { F::Idx<4> ix; L = F::decode_fast_any<4>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
+        else if (bs == 6) { F::Idx<6> ix; L = F::decode_fast_any<6>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
+        else { F::Idx<8> ix; L = F::decode_fast_any<8>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
+        if (L == 0) return 2;
+        for (int t = 0; t < N; ++t) {
+            const uint32_t k = (words[t >> 2] >> (8 * (t & 3))) & 0xFF;
+            if (k >= static_cast<uint32_t>(F::kTabCap)) return 3;
+            out[i * N + t] = __uint_as_float(tab[k]);
+        }
     }
     return 0;
 }
