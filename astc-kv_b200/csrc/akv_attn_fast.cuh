@@ -7,25 +7,30 @@
 //   * Staging: one elected thread issues cp.async.bulk copies of the chunk's
 //     V blocks and fp16 metadata (and ASTC K blocks) into a two-stage shared
 //     ring, completed on mbarriers; consumers wait with a bounded try_wait.
-//   * Decode (decode_plane_sorted): blocks are classified and counting-sorted
-//     by class so a warp's lanes share one code path; fast classes (single
-//     weight plane, full-resolution grid; akv_decode_fast.cuh) become a
-//     value table per block plus one index byte per texel, reduced-grid and
-//     dual-plane blocks get per-texel table entries computed one thread per
-//     texel. Table entries already hold v = scale*u + offset split into fp16
-//     hi and lo for block-affine planes. A thread per block row of texels
-//     then writes the padded [token][channel] hi/lo tiles.
-//   * Tensor cores (mma.sync m16n8k16, fp32 accumulation), one warp per 16
-//     tokens of the chunk, query heads of the GQA group as the N=8 dimension:
+//   * Decode (decode_plane): one thread per block with the runtime decoder of
+//     akv_decode_fast.cuh, the same instructions for every weight range and
+//     partition count (small machine code, no per-class divergence).
+//     Luminance blocks with a full-resolution grid become a value table
+//     (v = scale*u + offset split into fp16 hi and lo for block-affine
+//     planes) plus a weight-code byte per texel, and the thread writes its
+//     texels into the padded [token][channel] hi/lo tiles; reduced-grid,
+//     large-table and generic blocks become descriptors whose texels are
+//     evaluated one thread per texel afterwards.
+//   * Tensor cores (mma.sync m16n8k16, fp32 accumulation). Every warp owns
+//     one (16-token tile, half of the head dims) pair; the query heads of
+//     the GQA group are the N=8 dimension:
 //       S^T[tok][head] = K . Q^T   (q hi+lo; K fp16 straight from global
-//                                   memory in fragment order, or decoded
-//                                   K hi+lo from shared memory)
+//                                   memory in fragment order (L2-prefetched
+//                                   a chunk ahead), or decoded K hi+lo from
+//                                   shared memory; both warps of a tile
+//                                   compute it)
 //       online softmax per head in base 2, P^T as fp16 through a 256-byte
 //       per-warp buffer,
-//       O^T[dim][head] += V^T . P^T  (V hi and lo, ldmatrix.trans).
-//   * Each MMA warp keeps its own (m, l, O) over its token slices; the warps
-//     merge at the end and the CTA writes one split partial (m, l, acc), the
-//     same workspace format the merge kernel reads.
+//       O^T[dim][head] += V^T . P^T  for the warp's dim half (V hi and lo,
+//                                     ldmatrix.trans).
+//   * Each warp keeps its own (m, l, O half) over its token slices; the
+//     warps merge at the end and the CTA writes one split partial (m, l,
+//     acc), the same workspace format the merge kernel reads.
 #pragma once
 #include <math_constants.h>
 
@@ -92,6 +97,10 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -140,26 +149,60 @@ __device__ __forceinline__ int64_t meta_chunk_offset(int norm, int cols, int t_i
                                          : (norm == AKV_NORM_TOKEN ? t_in_page : 0);
 }
 
-// Scratch of the decode of one plane-chunk of up to NB blocks by NT threads.
-template <int NB, int NT>
+// Generic header decode for the rare blocks the runtime path does not cover
+// (kept out of line: it is large and rarely executed).
+template <int BS>
+__device__ __noinline__ void decode_header_slow(uint4 blk, BlockDesc<1>& d, uint8_t* w) {
+    decode_header<1>(blk, footprint_index(BS), d, w);
+}
+
+// One thread decodes and evaluates a whole block (beyond the slot capacity;
+// out of line, rarely executed).
+template <int BS, int LD>
+__device__ __noinline__ void eval_block_generic(uint4 blk, int norm, float sc, float of, const __half* moff,
+                                                const __half* mscl, int row0, int col0, int rows, int ncol,
+                                                __half (*thi)[LD], __half (*tlo)[LD]) {
+    BlockDesc<1> d;
+    uint8_t wl[64];
+    decode_header<1>(blk, footprint_index(BS), d, wl);
+    for (int t = 0; t < BS * BS; ++t) {
+        const int x = t % BS, y = t / BS;
+        if (x >= ncol) continue;
+        uint32_t cv[1];
+        texel_values<BS, 1>(d, wl, x, y, cv);
+        const float u = c16_to_unit(cv[0]);
+        float s = sc, o = of;
+        if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row0 + y]); o = __half2float(moff[row0 + y]); }
+        if (norm == AKV_NORM_PAGE_CHANNEL) { s = __half2float(mscl[col0 + x]); o = __half2float(moff[col0 + x]); }
+        const float v = fmaf(u, s, o);
+        const __half hv = __float2half_rn(v);
+        const bool ok = y < rows;
+        thi[row0 + y][col0 + x] = ok ? hv : __float2half_rn(0.f);
+        tlo[row0 + y][col0 + x] = ok ? __float2half_rn(v - __half2float(hv)) : __float2half_rn(0.f);
+    }
+}
+
+// Scratch of the decode of one plane-chunk of up to NB blocks by NT threads
+// (N = texels per block).
+template <int NB, int NT, int N>
 struct DecodeScratch {
-    static constexpr int kSlowCap = NB < 64 ? NB : 64;
-    int count[kNumKeys];        // first: the same counters for every plane sharing the scratch
+    static constexpr int kSlowCap = NB < 32 ? NB : 32;
     uint32_t tab[kTabCap][NT];  // value tables, thread-interleaved (conflict-free lookups)
-    uint16_t order[NB];         // block indices in key order
-    uint8_t key[NB];
+    uint8_t codes[N][NT];       // weight codes, thread-interleaved
+    int nslot;                  // descriptor slots taken in this plane-chunk
     uint16_t slow_blk[kSlowCap];
     BlockDesc<1> desc[kSlowCap];
     uint8_t w[kSlowCap][64];
 };
 
-// Texels of one table-decoded block -> the hi/lo tiles (pairs of columns per
-// 32-bit store). Rows at or past `rows` are written as zeros.
+// Texels of one table / constant block -> the hi/lo tiles (pairs of columns
+// per 32-bit store). Rows at or past `rows` are written as zeros.
 template <int BS, int LD>
-__device__ __forceinline__ void write_block(const Idx<BS>& ix, const uint32_t* tab, int nt, int norm,
-                                            const __half* moff, const __half* mscl, int row0, int col0, int rows,
-                                            int cols, __half (*thi)[LD], __half (*tlo)[LD]) {
+__device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt,
+                                            int norm, const __half* moff, const __half* mscl, int row0, int col0,
+                                            int rows, int cols, __half (*thi)[LD], __half (*tlo)[LD]) {
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
+    const uint32_t L = static_cast<uint32_t>(o.L);
 #pragma unroll
     for (int y = 0; y < BS; ++y) {
         const bool rok = y < rows;
@@ -172,9 +215,10 @@ __device__ __forceinline__ void write_block(const Idx<BS>& ix, const uint32_t* t
         for (int x = 0; x < BS; x += 2) {
             if (x < cols) {
                 const int i = y * BS + x;
-                const uint32_t i0 = (ix.w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-                const uint32_t i1 = (ix.w[(i + 1) >> 2] >> (8 * ((i + 1) & 3))) & 0xFFu;
-                const uint32_t a = tab[i0 * nt], b2 = tab[i1 * nt];
+                const uint32_t c0 = codes[i * nt] & o.cmask, c1 = codes[(i + 1) * nt] & o.cmask;
+                const uint32_t p0 = (o.pat[i >> 4] >> (2 * (i & 15))) & 3u;
+                const uint32_t p1 = (o.pat[(i + 1) >> 4] >> (2 * ((i + 1) & 15))) & 3u;
+                const uint32_t a = tab[(p0 * L + c0) * nt], b2 = tab[(p1 * L + c1) * nt];
                 uint32_t h, l;
                 if (affine) {
                     h = __byte_perm(a, b2, 0x5410);
@@ -204,59 +248,22 @@ __device__ __forceinline__ void put_texel(float v, bool ok, int row, int col, __
 }
 
 // Decode one plane's chunk into the hi/lo tiles. All threads call it.
-//   phase 0  key per block (fast weight range / constant / slow), ranks by
-//            warp-aggregated shared-memory atomics, scatter into key order;
-//   phase 1  thread per block in key order (lanes of a warp mostly share a
-//            code path): fast and constant blocks go straight to the tiles,
-//            slow blocks get their descriptor decoded;
-//   phase 1b thread per texel of the slow blocks.
+//   phase 1  thread per block: table and constant blocks go straight to the
+//            tiles; descriptor and generic blocks take a scratch slot;
+//   phase 1b thread per texel of the slotted blocks.
 template <int BS, int D, int THREADS, int NB, int LD>
 __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* moff, const __half* mscl, int norm,
                                              int cols, int rows_blk, int n, bool valid,
-                                             DecodeScratch<NB, THREADS>& ds, __half (*thi)[LD], __half (*tlo)[LD]) {
+                                             DecodeScratch<NB, THREADS, BS * BS>& ds, __half (*thi)[LD],
+                                             __half (*tlo)[LD]) {
     constexpr int N = BS * BS;
-    constexpr int fp = footprint_index(BS);
-    constexpr int PER = (NB + THREADS - 1) / THREADS;
-    constexpr int kCap = DecodeScratch<NB, THREADS>::kSlowCap;
+    constexpr int kCap = DecodeScratch<NB, THREADS, N>::kSlowCap;
     const int nblk = rows_blk * cols;
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
-    const int tid = threadIdx.x, lane = tid & 31;
-    // Phase 0: keys and ranks.
-    int rank[PER];
-#pragma unroll
-    for (int r = 0; r < PER; ++r) {
-        const int i = tid + r * THREADS;
-        rank[r] = -1;
-        if (i < nblk) {
-            const int k = block_key<BS>(raw[i]);
-            ds.key[i] = static_cast<uint8_t>(k);
-            const unsigned peers = __match_any_sync(__activemask(), k);
-            const int leader = __ffs(peers) - 1;
-            int base = 0;
-            if (lane == leader) base = atomicAdd(&ds.count[k], __popc(peers));
-            base = __shfl_sync(peers, base, leader);
-            rank[r] = base + __popc(peers & ((1u << lane) - 1u));
-        }
-    }
+    const int tid = threadIdx.x;
+    if (tid == 0) ds.nslot = 0;
     __syncthreads();
-    const int s0 = ds.count[kKeyConst];     // slow blocks sit at order[s0, s0 + nslow)
-    const int nslow = ds.count[kKeySlow];
-#pragma unroll
-    for (int r = 0; r < PER; ++r) {
-        if (rank[r] >= 0) {
-            const int i = tid + r * THREADS;
-            const int k = ds.key[i];
-            int base = 0;
-            for (int j = 0; j < k; ++j) base += ds.count[j];
-            ds.order[base + rank[r]] = static_cast<uint16_t>(i);
-        }
-    }
-    __syncthreads();
-    if (tid < kNumKeys) ds.count[tid] = 0;  // for the next plane-chunk (read after two more barriers)
-    // Phase 1.
-    for (int k = tid; k < nblk; k += THREADS) {
-        const int i = ds.order[k];
-        const int key = ds.key[i];
+    for (int i = tid; i < nblk; i += THREADS) {
         const uint4 blk = raw[i];
         const int br = i / cols, bc = i - br * cols;
         const int row0 = br * BS, col0 = bc * BS;
@@ -264,46 +271,34 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
         const int ncol = min(BS, D - col0);
         const float sc = affine ? __half2float(mscl[i]) : 0.f;
         const float of = affine ? __half2float(moff[i]) : 0.f;
-        uint32_t* tab = &ds.tab[0][tid];
-        if (key != kKeySlow) {
-            Idx<BS> ix;
-            if (key >= kKeyFast) {
-                decode_fast_any<BS>(key - kKeyFast, blk, affine, sc, of, tab, THREADS, ix);
-            } else {
-                tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
-#pragma unroll
-                for (int j = 0; j < Idx<BS>::NW; ++j) ix.w[j] = 0u;
+        uint32_t me;
+        int cq;
+        const int kind = block_kind<BS>(blk, me, cq);
+        int slot = -1;
+        if (kind == kKindDesc || kind == kKindGeneric) {
+            slot = atomicAdd(&ds.nslot, 1);
+            if (slot >= kCap) {
+                eval_block_generic<BS, LD>(blk, norm, sc, of, moff, mscl, row0, col0, rows, ncol, thi, tlo);
+                continue;
             }
-            write_block<BS, LD>(ix, tab, THREADS, norm, moff, mscl, row0, col0, rows, ncol, thi, tlo);
-            continue;
-        }
-        const int slot = k - s0;
-        if (slot < kCap) {
-            decode_header<1>(blk, fp, ds.desc[slot], ds.w[slot]);
             ds.slow_blk[slot] = static_cast<uint16_t>(i);
-            continue;
+            if (kind == kKindGeneric) {
+                decode_header_slow<BS>(blk, ds.desc[slot], ds.w[slot]);
+                continue;
+            }
         }
-        // Beyond the scratch capacity: evaluate the texels here.
-        BlockDesc<1> d;
-        uint8_t wl[64];
-        decode_header<1>(blk, fp, d, wl);
-#pragma unroll 1
-        for (int t = 0; t < N; ++t) {
-            const int x = t % BS, y = t / BS;
-            if (x >= ncol) continue;
-            uint32_t cv[1];
-            texel_values<BS, 1>(d, wl, x, y, cv);
-            const float u = c16_to_unit(cv[0]);
-            float s = sc, o = of;
-            if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row0 + y]); o = __half2float(moff[row0 + y]); }
-            if (norm == AKV_NORM_PAGE_CHANNEL) { s = __half2float(mscl[col0 + x]); o = __half2float(moff[col0 + x]); }
-            put_texel<LD>(fmaf(u, s, o), y < rows, row0 + y, col0 + x, thi, tlo);
-        }
+        LumOut o;
+        decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], THREADS,
+                       slot >= 0 ? &ds.desc[slot] : nullptr, slot >= 0 ? ds.w[slot] : nullptr, o);
+        if (slot < 0)
+            write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], THREADS, norm, moff, mscl, row0, col0, rows, ncol,
+                                thi, tlo);
     }
     __syncthreads();
+    const int nslow = min(ds.nslot, kCap);
     if (nslow > 0) {
-        // Phase 1b: texels of the slow blocks held in the scratch.
-        const int ntex = min(nslow, kCap) * N;
+        // Phase 1b: texels of the slotted blocks.
+        const int ntex = nslow * N;
         for (int task = tid; task < ntex; task += THREADS) {
             const int slot = task / N, t = task - slot * N;
             const int i = ds.slow_blk[slot];
@@ -329,7 +324,7 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
 template <int D, int G, int VBS, int KBS>
 struct Cfg {
     static constexpr int CH = (VBS == 6 || KBS == 6) ? 48 : 64;
-    static constexpr int NWM = CH / 16;                        // MMA warps
+    static constexpr int NWM = CH / 16;                        // token tiles of 16 per chunk
     static constexpr int THREADS = (VBS == 6) ? 192 : 256;
     static constexpr int LD = D + 8;                           // halves per tile row (16-byte pad)
     static constexpr int VCOLS = (D + VBS - 1) / VBS;
@@ -342,8 +337,8 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS>);
-    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS>) : 0;
+    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS * VBS>);
+    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 1) * (KBS ? KBS : 1)>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
@@ -364,7 +359,7 @@ struct Smem {
     __align__(16) __half khi[KBS ? C::CH : 1][C::LD];
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
-    __align__(16) __half pbuf[C::NWM][8][16];
+    __align__(16) __half pbuf[2 * C::NWM][8][16];
     __align__(16) uint4 qfrag[D / 16][32];                         // per lane: q hi (2 words) | q lo (2 words)
 
     float wm[C::NWM][8];
@@ -376,6 +371,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
     using C = Cfg<D, G, VBS, KBS>;
     using S = Smem<D, G, VBS, KBS>;
     constexpr int CH = C::CH, NWM = C::NWM, THREADS = C::THREADS, LD = C::LD;
+    static_assert(THREADS == 64 * NWM, "every warp owns one (token tile, dim half)");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     S& sm = *reinterpret_cast<S*>(smem_raw);
 
@@ -402,7 +398,6 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         mbar_init(&sm.bar[1], 1);
         fence_mbar_init();
     }
-    if (tid < kNumKeys) reinterpret_cast<DecodeScratch<C::VBLK, THREADS>*>(sm.ds)->count[tid] = 0;
     __syncthreads();
 
     // Producer: stage `s` <- chunk `c` (one elected thread).
@@ -469,6 +464,8 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
     // group, computed once by warp 0 into shared memory.
     const int qn = lane >> 2, qj = lane & 3;
     constexpr int KS = D / 16;
+    constexpr int KH = KS / 2;  // dim tiles per half
+    const int tw = warp % NWM, dh = warp / NWM;
     if (warp == 0) {
         const bool has = qn < G;
         const int64_t qb = (static_cast<int64_t>(b) * p.Hq + h * G + (has ? qn : 0)) * D;
@@ -490,9 +487,24 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         }
     }
 
-    float o[KS][4];
+    auto prefetch_k = [&](int c) {
+        if constexpr (KBS == 0) {
+            if (dh == 0 && c < nchunks) {
+                const int tt = t_begin + c * CH + 16 * tw + (lane >> 1);
+                if (tt < t_end && (lane & 1) * 128 < D * 2) {
+                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
+                    if (phys >= 0)
+                        prefetch_l2(p.k.data + b * p.k.sB + h * p.k.sH + static_cast<int64_t>(phys) * p.k.sP +
+                                    static_cast<int64_t>(tt % P) * D * 2 + (lane & 1) * 128);
+                }
+            }
+        }
+    };
+    prefetch_k(0);
+
+    float o[KH][4];
 #pragma unroll
-    for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    for (int i = 0; i < KH; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F}, l_run[2] = {0.f, 0.f};
     bool stuck = false;
 
@@ -507,16 +519,17 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
             break;
         }
         const bool valid = sm.valid[s] != 0;
+        prefetch_k(c + 1);
         // Decode V (and K) tiles.
         decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
                                                   CH / VBS, n, valid,
-                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS>*>(sm.ds), sm.vhi,
+                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS * VBS>*>(sm.ds), sm.vhi,
                                                   sm.vlo);
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
             decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
-                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS>*>(sm.ds),
+                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS, KB * KB>*>(sm.ds),
                                                 sm.khi, sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;
@@ -539,10 +552,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         // 32-dim group g.
         uint4 kreg[KBS ? 1 : D / 32][2];
         if constexpr (KBS == 0) {
-            if (warp < NWM) {
+            {
 #pragma unroll
                 for (int rr = 0; rr < 2; ++rr) {
-                    const int tr = 16 * warp + qn + 8 * rr;
+                    const int tr = 16 * tw + qn + 8 * rr;
                     const int tt = t0 + tr;
                     const uint4* row = nullptr;
                     if (tr < n) {
@@ -563,8 +576,9 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
             fence_proxy_async();
             issue(c + 2, s);
         }
-        // Tensor-core phase: warp w owns chunk tokens [16w, 16w + 16).
-        if (warp < NWM) {
+        // Tensor-core phase: warp w owns chunk tokens [16 tw, 16 tw + 16) and
+        // dim half dh (both warps of a token tile compute its scores).
+        {
             __syncwarp();
             // Two independent accumulator chains (even / odd k-steps).
             float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -575,7 +589,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
                 uint32_t a[4];
                 if constexpr (KBS > 0) {
                     const int mi = lane >> 3, rr = lane & 7;
-                    const int row = 16 * warp + rr + ((mi & 1) ? 8 : 0);
+                    const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
                     const int col = 16 * ks + ((mi & 2) ? 8 : 0);
                     ldsm_x4(a, &sm.khi[row][col]);
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
@@ -595,7 +609,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
 #pragma unroll
             for (int i = 0; i < 4; ++i) sacc[i] = sa[0][i] + sa[1][i];
             // sacc: S^T[tok = qn (+8)][head = 2qj (+1)], in log2 units after scaling.
-            const bool v0 = 16 * warp + qn < n, v1 = 16 * warp + qn + 8 < n;
+            const bool v0 = 16 * tw + qn < n, v1 = 16 * tw + qn + 8 < n;
             float sv[4];
             sv[0] = v0 ? sacc[0] * p.qscale : -CUDART_INF_F;
             sv[1] = v0 ? sacc[1] * p.qscale : -CUDART_INF_F;
@@ -623,7 +637,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
                 m_run[j] = mn;
             }
 #pragma unroll
-            for (int i = 0; i < KS; ++i) {
+            for (int i = 0; i < KH; ++i) {
                 o[i][0] *= alpha[0];
                 o[i][1] *= alpha[1];
                 o[i][2] *= alpha[0];
@@ -640,14 +654,15 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
             const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&pb[qn][2 * qj + 8]);
             // O^T[dim][head] += V^T . P^T with V = hi + lo.
             const int mi = lane >> 3, rr = lane & 7;
-            const int vrow = 16 * warp + rr + ((mi & 2) ? 8 : 0);
+            const int vrow = 16 * tw + rr + ((mi & 2) ? 8 : 0);
             const int vcol = (mi & 1) ? 8 : 0;
 #pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
+            for (int mt = 0; mt < KH; ++mt) {
+                const int dt = dh * KH + mt;
                 uint32_t a[4];
-                ldsm_x4_t(a, &sm.vhi[vrow][16 * mt + vcol]);
+                ldsm_x4_t(a, &sm.vhi[vrow][16 * dt + vcol]);
                 mma16816(o[mt], a[0], a[1], a[2], a[3], b0, b1);
-                ldsm_x4_t(a, &sm.vlo[vrow][16 * mt + vcol]);
+                ldsm_x4_t(a, &sm.vlo[vrow][16 * dt + vcol]);
                 mma16816(o[mt], a[0], a[1], a[2], a[3], b0, b1);
             }
             __syncwarp();
@@ -674,14 +689,14 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
     // Merge the MMA warps' (m, l, O) into one split partial.
     float* red = reinterpret_cast<float*>(&sm.vhi[0][0]);  // G * D floats, fits in the V tiles
     for (int i = tid; i < G * D; i += THREADS) red[i] = 0.f;
-    if (warp < NWM && lane < 4) {
-        sm.wm[warp][2 * lane] = m_run[0];
-        sm.wm[warp][2 * lane + 1] = m_run[1];
-        sm.wl[warp][2 * lane] = l_run[0];
-        sm.wl[warp][2 * lane + 1] = l_run[1];
+    if (dh == 0 && lane < 4) {
+        sm.wm[tw][2 * lane] = m_run[0];
+        sm.wm[tw][2 * lane + 1] = m_run[1];
+        sm.wl[tw][2 * lane] = l_run[0];
+        sm.wl[tw][2 * lane + 1] = l_run[1];
     }
     __syncthreads();
-    if (warp < NWM) {
+    {
         float scl[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -692,8 +707,8 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
             scl[j] = (M == -CUDART_INF_F || m_run[j] == -CUDART_INF_F) ? 0.f : exp2f(m_run[j] - M);
         }
 #pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-            const int d0 = 16 * mt + qn;
+        for (int mt = 0; mt < KH; ++mt) {
+            const int d0 = 16 * (dh * KH + mt) + qn;
             if (2 * qj < G) {
                 atomicAdd(&red[(2 * qj) * D + d0], o[mt][0] * scl[0]);
                 atomicAdd(&red[(2 * qj) * D + d0 + 8], o[mt][2] * scl[0]);

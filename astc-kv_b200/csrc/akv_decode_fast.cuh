@@ -1,10 +1,16 @@
-// Per-block "value table" decode of scalar-layout ASTC blocks (R channel),
-// used by the sorted decode of akv_attn_fast.cuh.
+// Runtime-parameterised decode of scalar-layout ASTC blocks (R channel) for
+// the fused attention kernel (akv_attn_fast.cuh).
 //
-// Fast-class blocks (single weight plane, full-resolution grid, table small
-// enough) become a table of values indexed by partition * levels + weight
-// code plus one index byte per texel; every BISE position is a compile-time
-// constant because the weight range is a template parameter.
+// One compact code path serves every weight range, partition count and
+// footprint: per-range quantities (bits per value, trit/quint groups, group
+// widths) are runtime values, so the lanes of a warp run the same
+// instructions whatever their blocks look like and the kernel's machine code
+// stays small. A luminance-direct (endpoint mode 0), single-plane block with
+// a full-resolution grid becomes a value table (entry = partition * levels +
+// weight code, affine and fp16 hi/lo split folded in) plus one weight-code
+// byte per texel; with a reduced grid, or a table larger than kTabCap, it
+// becomes a descriptor evaluated per texel. Everything else takes the
+// generic decoder of akv_astc_device.cuh.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -12,6 +18,12 @@
 
 namespace akv {
 namespace fast {
+
+// Value-table capacity per block (entries = partitions * weight levels).
+constexpr int kTabCap = 24;
+
+// Block kinds of the runtime path.
+enum : int { kKindTable = 0, kKindDesc = 1, kKindGeneric = 2, kKindConst = 3 };
 
 __device__ __forceinline__ int range_levels(int q) {
     const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
@@ -27,46 +39,6 @@ __device__ __forceinline__ uint32_t table_entry(float u, bool affine, float sc, 
     const __half hi = __float2half_rn(v);
     const __half lo = __float2half_rn(v - __half2float(hi));
     return static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
-}
-
-// Weight unquantisation (spec formula) evaluated at compile time for a
-// compile-time weight range, so value tables need no table loads.
-constexpr int cx_replicate(int v, int n, int width) {
-    int out = 0, filled = 0;
-    while (filled < width) {
-        const int k = n < width - filled ? n : width - filled;
-        out = (out << k) | (v >> (n - k));
-        filled += k;
-    }
-    return out;
-}
-
-constexpr int cx_weight(int q, int code) {
-    const int lv[12] = {2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32};
-    const int L = lv[q];
-    const bool tr = L % 3 == 0, qu = L % 5 == 0;
-    const int base = tr ? L / 3 : (qu ? L / 5 : L);
-    int b = 0;
-    while ((1 << b) < base) ++b;
-    int r = 0;
-    if (!tr && !qu) {
-        r = cx_replicate(code, b, 6);
-    } else if (b == 0) {
-        r = tr ? (code == 0 ? 0 : code == 1 ? 32 : 63) : (code * 16 - (code >= 3 ? 1 : 0));
-    } else {
-        const int digit = code >> b, m = code & ((1 << b) - 1);
-        const int a = m & 1, bb = (m >> 1) & 1, c = (m >> 2) & 1;
-        int B = 0, C = 0;
-        if (L == 6) C = 50;
-        else if (L == 10) C = 28;
-        else if (L == 12) { C = 23; B = bb * 0x45; }
-        else if (L == 20) { C = 13; B = bb * 0x42; }
-        else if (L == 24) { C = 11; B = c * 0x42 + bb * 0x21; }
-        const int A = a ? 0x7F : 0;
-        const int T = (digit * C + B) ^ A;
-        r = (A & 0x20) | (T >> 2);
-    }
-    return r > 32 ? r + 1 : r;
 }
 
 // Up to eight colour integers of range `cq` from a colour stream that starts
@@ -122,39 +94,6 @@ __device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int 
     }
 }
 
-// Value-table capacity per block (entries = partitions * weight levels).
-constexpr int kTabCap = 32;
-
-// Sort keys of the per-chunk counting sort: constant blocks, per-texel
-// ("slow") blocks, and one key per weight range for fast blocks.
-constexpr int kKeyConst = 0;
-constexpr int kKeySlow = 1;
-constexpr int kKeyFast = 2;  // + weight range index 0..11
-constexpr int kNumKeys = 14;
-
-// Sort key of a block. Fast blocks: one weight plane, full-resolution grid,
-// luminance-direct endpoints (mode 0) on every partition and a value table
-// of at most kTabCap entries. Constant: void extent or an illegal encoding
-// (error colour).
-template <int BS>
-__device__ __forceinline__ int block_key(uint4 blk) {
-    constexpr int fp = footprint_index(BS);
-    const uint32_t x = blk.x;
-    const int mode = static_cast<int>(x & 0x7FF);
-    if ((mode & 0x1FF) == 0x1FC) return kKeyConst;
-    const uint32_t me = __ldg(&g_akv_tables.mode[fp][mode]);
-    if (!(me & kModeValid)) return kKeyConst;
-    if (me & (kModeDual | kModeReduced)) return kKeySlow;
-    const int parts = static_cast<int>((x >> 11) & 3) + 1;
-    const bool lum = parts == 1 ? ((x >> 13) & 15) == 0 : ((x >> 23) & 0x3F) == 0;
-    if (!lum) return kKeySlow;
-    const int wq = mode_wq(me);
-    const int avail = 128 - mode_wbits(me) - (parts == 1 ? 17 : 29);
-    if (avail < 0 || __ldg(&g_akv_tables.cquant[parts][avail]) == 0xFF) return kKeyConst;
-    if (parts * range_levels(wq) > kTabCap) return kKeySlow;
-    return kKeyFast + wq;
-}
-
 // UNORM16 value of a constant block: the void-extent R colour, or the error
 // colour's R = 1.0 for illegal encodings.
 __device__ __forceinline__ uint32_t const_c16(uint4 blk) {
@@ -170,55 +109,90 @@ __device__ __forceinline__ uint32_t const_c16(uint4 blk) {
     return 0xFFFFu;
 }
 
-// Per-texel table-index bytes of one block (texel t in byte t & 3 of word t >> 2).
+// Kind of a block, with its mode-table entry and colour range for the
+// luminance kinds (table / descriptor).
 template <int BS>
-struct Idx {
-    static constexpr int NW = (BS * BS + 3) / 4;
-    uint32_t w[NW];
-};
-
-// Fast block of weight range WQ (every BISE position is a compile-time
-// constant): endpoints, value table (entry q * L + code at tab[entry * nt])
-// and the per-texel index bytes q * L + code. Returns L.
-template <int BS, int WQ>
-__device__ __forceinline__ int decode_fast(uint4 blk, bool affine, float sc, float of, uint32_t* tab, int nt,
-                                           Idx<BS>& ix) {
+__device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
     constexpr int fp = footprint_index(BS);
-    constexpr int N = BS * BS;
-    constexpr int NW = Idx<BS>::NW;
-    constexpr int kLv[12] = {2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32};
-    constexpr int L = kLv[WQ];
-    constexpr bool TR = (L % 3) == 0;
-    constexpr bool QU = (L % 5) == 0;
-    constexpr int B = TR ? (L == 3 ? 0 : L == 6 ? 1 : L == 12 ? 2 : 3)
-                         : QU ? (L == 5 ? 0 : L == 10 ? 1 : 2)
-                              : (L == 2 ? 1 : L == 4 ? 2 : L == 8 ? 3 : L == 16 ? 4 : 5);
-    constexpr int WBITS = N * B + (TR ? (8 * N + 4) / 5 : 0) + (QU ? (7 * N + 2) / 3 : 0);
+    const uint32_t x = blk.x;
+    const int mode = static_cast<int>(x & 0x7FF);
+    me = 0u;
+    cq = 0;
+    if ((mode & 0x1FF) == 0x1FC) return kKindConst;
+    me = __ldg(&g_akv_tables.mode[fp][mode]);
+    if (!(me & kModeValid)) return kKindConst;
+    if (me & kModeDual) return kKindGeneric;
+    const int parts = static_cast<int>((x >> 11) & 3) + 1;
+    const bool lum = parts == 1 ? ((x >> 13) & 15) == 0 : ((x >> 23) & 0x3F) == 0;
+    if (!lum) return kKindGeneric;
+    const int avail = 128 - mode_wbits(me) - (parts == 1 ? 17 : 29);
+    cq = avail < 0 ? 0xFF : __ldg(&g_akv_tables.cquant[parts][avail]);
+    if (cq == 0xFF) return kKindConst;
+    if ((me & kModeReduced) || parts * range_levels(mode_wq(me)) > kTabCap) return kKindDesc;
+    return kKindTable;
+}
+
+// BISE weight codes: `count` values of range wq from the bit-reversed weight
+// stream (s0, s1), already masked to its length, into codes[i * nt]. Groups
+// of five (trits, plain bits) or three (quints) values per step, with the
+// trit/quint block bits gathered by runtime shifts and decoded through the
+// combined digit table.
+__device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, int count, uint8_t* codes, int nt) {
     const Tables& T = g_akv_tables;
-    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
-    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
-    const int parts = static_cast<int>((lo >> 11) & 3) + 1;
-    const int seed = static_cast<int>((lo >> 13) & 0x3FF);
-    const int cstart = parts == 1 ? 17 : 29;
-    const int cq = T.cquant[parts][128 - WBITS - cstart];
-    // Luminance-direct endpoints: e0 = v[2q], e1 = v[2q + 1].
-    int v[8];
-    {
-        uint64_t clo = window_u128(lo, hi, cstart);
-        uint64_t chi = hi >> cstart;
-        mask_u128(clo, chi, bise_stream_bits_dev(2 * parts, cq));
-        colors8(clo, chi, cq, v);
+    const uint32_t shp = __ldg(&T.shape[wq]);
+    const int b = shp & 15;
+    const bool tr = (shp >> 4) & 1, qu = (shp >> 5) & 1;
+    const int gs = qu ? 3 : 5;
+    const int gb = tr ? 5 * b + 8 : (qu ? 3 * b + 7 : 5 * b);
+    const int ng = qu ? (count + 2) / 3 : (count + 4) / 5;
+    // Masks of the trit / quint block bits after shifting by k * b.
+    const uint32_t m1 = tr ? 0x03u : (qu ? 0x07u : 0u);
+    const uint32_t m2 = tr ? 0x0Cu : (qu ? 0x18u : 0u);
+    const uint32_t m3 = tr ? 0x10u : (qu ? 0x60u : 0u);
+    const uint32_t m4 = tr ? 0x60u : 0u;
+    const uint32_t m5 = tr ? 0x80u : 0u;
+    // Offsets of the low bits of values 1..4 within a group.
+    const int o1 = b + (tr ? 2 : (qu ? 3 : 0));
+    const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
+    const int o3 = 3 * b + (tr ? 5 : 0);
+    const int o4 = 4 * b + (tr ? 7 : 0);
+    const int dbase = qu ? 256 : 0;
+    const uint32_t bm = (1u << b) - 1u;
+    uint8_t* cp = codes;
+    int left = count;
+    for (int g = 0; g < ng; ++g) {
+        const uint32_t win = static_cast<uint32_t>(s0);
+        const uint32_t X = ((win >> b) & m1) | ((win >> (2 * b)) & m2) | ((win >> (3 * b)) & m3) |
+                           ((win >> (4 * b)) & m4) | ((win >> (5 * b)) & m5);
+        const uint32_t dg = __ldg(&T.dig3[dbase + X]);
+        cp[0] = static_cast<uint8_t>(((dg & 7u) << b) | (win & bm));
+        if (left > 1) cp[nt] = static_cast<uint8_t>((((dg >> 3) & 7u) << b) | ((win >> o1) & bm));
+        if (left > 2) cp[2 * nt] = static_cast<uint8_t>((((dg >> 6) & 7u) << b) | ((win >> o2) & bm));
+        if (!qu) {
+            if (left > 3) cp[3 * nt] = static_cast<uint8_t>((((dg >> 9) & 7u) << b) | ((win >> o3) & bm));
+            if (left > 4) cp[4 * nt] = static_cast<uint8_t>((((dg >> 12) & 7u) << b) | ((win >> o4) & bm));
+        }
+        cp += gs * nt;
+        left -= gs;
+        s0 = (s0 >> gb) | (s1 << (64 - gb));
+        s1 >>= gb;
     }
-    // Value table, two entries per step (fp16 hi/lo packing on pairs).
+}
+
+// Value table of a luminance-direct block: entry q * L + code at
+// tab[entry * nt], two entries per step (fp16 hi/lo packing on pairs).
+__device__ __forceinline__ void build_table(const int (&v)[8], int parts, int wq, int L, bool affine, float sc,
+                                            float of, uint32_t* tab, int nt) {
+    const uint8_t* wun = g_akv_tables.wunq[wq];
     const float s16 = sc * 0x1p-16f;  // u = t * 2^-16 with t = C truncated to 11 significant bits
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         if (q < parts) {
             const int e0 = v[2 * q], e1 = v[2 * q + 1];
-#pragma unroll
-            for (int code = 0; code < L; code += 2) {
-                const int wa = cx_weight(WQ, code);
-                const int wb = cx_weight(WQ, code + 1 < L ? code + 1 : code);
+            uint32_t* tq = tab + q * L * nt;
+            for (int c = 0; c < L; c += 2) {
+                const uint32_t wpair = __ldg(reinterpret_cast<const uint16_t*>(wun + c));
+                const int wa = static_cast<int>(wpair & 0xFF), wb = static_cast<int>(wpair >> 8);
                 const uint32_t ca = static_cast<uint32_t>(257 * (e0 * (64 - wa) + e1 * wa) + 32) >> 6;
                 const uint32_t cb = static_cast<uint32_t>(257 * (e0 * (64 - wb) + e1 * wb) + 32) >> 6;
                 // 65535 decodes to exactly 1.0 (t = 65536).
@@ -238,152 +212,86 @@ __device__ __forceinline__ int decode_fast(uint4 blk, bool affine, float sc, flo
                     e_a = __float_as_uint(ta * 0x1p-16f);
                     e_b = __float_as_uint(tb * 0x1p-16f);
                 }
-                tab[(q * L + code) * nt] = e_a;
-                if (code + 1 < L) tab[(q * L + code + 1) * nt] = e_b;
+                tq[c * nt] = e_a;
+                if (c + 1 < L) tq[(c + 1) * nt] = e_b;
             }
         }
     }
-    // Weight stream (bit-reversed, masked) and partition pattern.
-    uint64_t w0 = __brevll(hi), w1 = __brevll(lo);
-    mask_u128(w0, w1, WBITS);
-    uint32_t pat[4] = {0u, 0u, 0u, 0u};
-    if (parts > 1) {
-        const uint32_t* pt = T.part[fp][parts - 2][seed];
-#pragma unroll
-        for (int k = 0; k < (N + 15) / 16; ++k) pat[k] = __ldg(pt + k);
-    }
-    auto wbits = [&](int pos, int n) -> uint32_t {  // pos, n compile-time after unrolling
-        const uint64_t u = pos >= 64 ? (w1 >> (pos - 64)) : (pos == 0 ? w0 : ((w0 >> pos) | (w1 << (64 - pos))));
-        return static_cast<uint32_t>(u) & ((n >= 32) ? 0xFFFFFFFFu : ((1u << n) - 1u));
-    };
-    uint32_t* cw = ix.w;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) cw[k] = 0u;
-    constexpr bool kSwar = (L == 2 || L == 3 || L == 4 || L == 5 || L == 6);
-    if constexpr (kSwar) {
-        // Weight codes become index bytes four or more at a time through
-        // host-built spread tables; partition * L is added per word.
-        uint32_t ext[3] = {0u, 0u, 0u};  // spill-over words past NW
-        auto word = [&](int k) -> uint32_t& { return k < NW ? cw[k < NW ? k : 0] : ext[k - NW < 3 ? k - NW : 0]; };
-        // OR `nb` code bytes (value u) in at texel offset `off` (compile time).
-        auto place = [&](int off, uint64_t u, int nb) {
-            const int k = off >> 2, o = off & 3;
-            if (o == 0) {
-                word(k) |= static_cast<uint32_t>(u);
-                if (nb > 4) word(k + 1) |= static_cast<uint32_t>(u >> 32);
-            } else {
-                const uint64_t t = u << (8 * o);
-                word(k) |= static_cast<uint32_t>(t);
-                if (nb + o > 4) word(k + 1) |= static_cast<uint32_t>(t >> 32);
-                if (nb + o > 8) word(k + 2) |= static_cast<uint32_t>(u >> (64 - 8 * o));
-            }
-        };
-        if constexpr (L == 4) {
-#pragma unroll
-            for (int k = 0; k < NW; ++k) cw[k] = __ldg(&T.spread2[wbits(8 * k, 8)]);
-        } else if constexpr (L == 2) {
-#pragma unroll
-            for (int g = 0; g < (N + 7) / 8; ++g) place(8 * g, __ldg(&T.spread1[wbits(8 * g, 8)]), 8);
-        } else if constexpr (L == 3) {
-#pragma unroll
-            for (int g = 0; g < (N + 4) / 5; ++g) place(5 * g, __ldg(&T.tlut[wbits(8 * g, 8)]), 5);
-        } else if constexpr (L == 5) {
-#pragma unroll
-            for (int g = 0; g < (N + 2) / 3; ++g) place(3 * g, __ldg(&T.qlut[wbits(7 * g, 7)]), 3);
-        } else if constexpr (L == 6) {
-#pragma unroll
-            for (int g = 0; g < (N + 4) / 5; ++g) {
-                const uint32_t bits13 = wbits(13 * g, 13);
-                const uint64_t c = __ldg(&T.t13lo[bits13 & 0x7F]) | __ldg(&T.t13hi[bits13 >> 7]);
-                const uint64_t d5 = __ldg(&T.tlut[static_cast<uint32_t>(c >> 56)]);
-                place(5 * g, (d5 << 1) | (c & 0xFFFFFFFFFFull), 5);
-            }
-        }
-        if (N % 4) cw[NW - 1] &= (1u << (8 * (N % 4))) - 1u;
-        if (parts > 1) {
-#pragma unroll
-            for (int k = 0; k < NW; ++k) cw[k] += __ldg(&T.spread2[(pat[k >> 2] >> (8 * (k & 3))) & 0xFF]) * L;
-        }
-        return L;
-    }
-    auto emit = [&](int i, int code) {
-        const int part = (pat[i >> 4] >> (2 * (i & 15))) & 3;
-        cw[i >> 2] |= static_cast<uint32_t>(part * L + code) << (8 * (i & 3));
-    };
-    if constexpr (TR) {
-        constexpr int GB = 5 * B + 8;
-#pragma unroll
-        for (int g = 0; g < (N + 4) / 5; ++g) {
-            const int base = g * GB;
-            const uint32_t tbits = wbits(base + B, 2) | (wbits(base + 2 * B + 2, 2) << 2) |
-                                   (wbits(base + 3 * B + 4, 1) << 4) | (wbits(base + 4 * B + 5, 2) << 5) |
-                                   (wbits(base + 5 * B + 7, 1) << 7);
-            const uint32_t dg = __ldg(&T.trit[tbits]);
-            constexpr int off[5] = {0, 2, 4, 5, 7};
-#pragma unroll
-            for (int j = 0; j < 5; ++j) {
-                const int i = 5 * g + j;
-                if (i < N) emit(i, static_cast<int>((((dg >> (2 * j)) & 3u) << B) | (B ? wbits(base + j * B + off[j], B) : 0u)));
-            }
-        }
-    } else if constexpr (QU) {
-        constexpr int GB = 3 * B + 7;
-#pragma unroll
-        for (int g = 0; g < (N + 2) / 3; ++g) {
-            const int base = g * GB;
-            const uint32_t qbits = wbits(base + B, 3) | (wbits(base + 2 * B + 3, 2) << 3) | (wbits(base + 3 * B + 5, 2) << 5);
-            const uint32_t dg = __ldg(&T.quint[qbits]);
-            constexpr int off[3] = {0, 3, 5};
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const int i = 3 * g + j;
-                if (i < N) emit(i, static_cast<int>((((dg >> (3 * j)) & 7u) << B) | (B ? wbits(base + j * B + off[j], B) : 0u)));
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < N; ++i) emit(i, static_cast<int>(wbits(i * B, B)));
-    }
-    return L;
 }
 
-// Per-key dispatch of the fast decode (only the weight ranges a footprint can
-// use with a full-resolution grid are instantiated). Returns L, or 0 for a
-// range that cannot occur (the caller then treats the block as slow).
+// What the tile writer needs of a table / constant block.
+struct LumOut {
+    uint32_t pat[4];  // partition per texel, 2 bits each
+    int L;            // table entries per partition
+    uint32_t cmask;   // 0xFF, or 0 for a constant block (every texel -> entry 0)
+};
+
+// Runtime path for table, descriptor and constant blocks (kind from
+// block_kind). Table / constant: tab and codes filled, `o` describes them.
+// Descriptor: *d and w filled as decode_header fills them (codes used as
+// scratch).
 template <int BS>
-__device__ __forceinline__ int decode_fast_any(int wq, uint4 blk, bool affine, float sc, float of, uint32_t* tab,
-                                               int nt, Idx<BS>& ix) {
+__device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int cq, bool affine, float sc, float of,
+                                           uint32_t* tab, uint8_t* codes, int nt, BlockDesc<1>* d, uint8_t* w,
+                                           LumOut& o) {
+    constexpr int fp = footprint_index(BS);
     constexpr int N = BS * BS;
-    // WQ valid for a full grid iff its stream fits in 24..96 bits.
-#define AKV_FAST_CASE(Q)                                                                                 \
-    case Q: {                                                                                            \
-        constexpr int kL[12] = {2, 3, 4, 5, 6, 8, 10, 12, 16, 20, 24, 32};                               \
-        constexpr int L = kL[Q];                                                                         \
-        constexpr int bb = (L % 3 == 0) ? (L == 3 ? 0 : L == 6 ? 1 : L == 12 ? 2 : 3)                     \
-                           : (L % 5 == 0) ? (L == 5 ? 0 : L == 10 ? 1 : 2)                                \
-                                          : (L == 2 ? 1 : L == 4 ? 2 : L == 8 ? 3 : L == 16 ? 4 : 5);     \
-        constexpr int wb = N * bb + ((L % 3 == 0) ? (8 * N + 4) / 5 : 0) + ((L % 5 == 0) ? (7 * N + 2) / 3 : 0); \
-        if constexpr (wb >= 24 && wb <= 96) return decode_fast<BS, Q>(blk, affine, sc, of, tab, nt, ix);  \
-        return 0;                                                                                        \
+    const Tables& T = g_akv_tables;
+    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
+    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
+    const bool lum = kind != kKindConst;
+    const int parts = lum ? static_cast<int>((lo >> 11) & 3) + 1 : 1;
+    const int wq = mode_wq(me);
+    const int L = lum ? range_levels(wq) : 1;
+    o.L = L;
+    o.cmask = lum ? 0xFFu : 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o.pat[k] = 0u;
+    if (!lum) {
+        tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+        return;
     }
-    switch (wq) {
-        AKV_FAST_CASE(0) AKV_FAST_CASE(1) AKV_FAST_CASE(2) AKV_FAST_CASE(3) AKV_FAST_CASE(4) AKV_FAST_CASE(5)
-        AKV_FAST_CASE(6) AKV_FAST_CASE(7) AKV_FAST_CASE(8) AKV_FAST_CASE(9) AKV_FAST_CASE(10) AKV_FAST_CASE(11)
-        default: return 0;
+    int v[8];
+    {
+        const int cstart = parts == 1 ? 17 : 29;
+        uint64_t clo = window_u128(lo, hi, cstart);
+        uint64_t chi = hi >> cstart;
+        mask_u128(clo, chi, bise_stream_bits_dev(2 * parts, cq));
+        colors8(clo, chi, cq, v);
     }
-#undef AKV_FAST_CASE
+    if (kind == kKindTable) build_table(v, parts, wq, L, affine, sc, of, tab, nt);
+    if (parts > 1) {
+        const uint32_t* pt = T.part[fp][parts - 2][(lo >> 13) & 0x3FF];
+#pragma unroll
+        for (int k = 0; k < (N + 15) / 16; ++k) o.pat[k] = __ldg(pt + k);
+    }
+    const int wx = mode_wx(me), wy = mode_wy(me);
+    const int count = wx * wy;
+    {
+        uint64_t s0 = __brevll(hi), s1 = __brevll(lo);
+        mask_u128(s0, s1, mode_wbits(me));
+        weight_codes(s0, s1, wq, count, codes, nt);
+    }
+    if (kind == kKindDesc) {
+        const uint8_t* un = T.wunq[wq];
+        for (int j = 0; j < count; ++j) w[j] = __ldg(un + codes[j * nt]);
+        d->pat[0] = o.pat[0];
+        d->pat[1] = o.pat[1];
+        d->pat_hi[0] = o.pat[2];
+        d->pat_hi[1] = o.pat[3];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d->ep[q] = q < parts ? static_cast<uint32_t>(v[2 * q] | (v[2 * q + 1] << 8)) : 0u;
+        d->info = static_cast<uint32_t>(parts - 1) | ((me & kModeReduced) ? (1u << kInfoReduced) : 0u) |
+                  (static_cast<uint32_t>(wx) << kInfoWx) | (static_cast<uint32_t>(wy) << kInfoWy);
+    }
 }
 
-// Texel value of a table entry as fp32: block-affine entries hold v as fp16
-// hi | lo << 16, the others the unit value u (the caller applies the
-// per-token / per-channel affine).
-__device__ __forceinline__ float entry_value(uint32_t e, bool affine) {
-    if (affine) {
-        const __half2 h = *reinterpret_cast<const __half2*>(&e);
-        const float2 f = __half22float2(h);
-        return f.x + f.y;
-    }
-    return __uint_as_float(e);
+// fp32 value of texel t of a table / constant block (host emulation and
+// checks; the kernel's tile writer reads the same table).
+__device__ __forceinline__ float lum_unit(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt, int t) {
+    const uint32_t c = codes[t * nt] & o.cmask;
+    const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
+    return __uint_as_float(tab[(part * o.L + c) * nt]);
 }
 
 }  // namespace fast

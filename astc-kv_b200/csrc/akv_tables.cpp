@@ -245,33 +245,13 @@ void build_tables(Tables* t) {
                 if (bise_stream_bits(2 * pairs, q) <= avail) { pick = static_cast<uint8_t>(q); break; }
             t->cquant[pairs][avail] = pick;
         }
+    // Combined digit table, 3 bits per digit: trit blocks, then quint blocks.
     for (int v = 0; v < 256; ++v) {
-        uint32_t a = 0;
-        uint64_t b1 = 0;
-        for (int k = 0; k < 4; ++k) a |= static_cast<uint32_t>((v >> (2 * k)) & 3) << (8 * k);
-        for (int k = 0; k < 8; ++k) b1 |= static_cast<uint64_t>((v >> k) & 1) << (8 * k);
-        t->spread2[v] = a;
-        t->spread1[v] = b1;
-        uint64_t tl = 0;
-        for (int j = 0; j < 5; ++j) tl |= static_cast<uint64_t>((t->trit[v] >> (2 * j)) & 3) << (8 * j);
-        t->tlut[v] = tl;
+        uint16_t d = 0;
+        for (int j = 0; j < 5; ++j) d |= static_cast<uint16_t>(((t->trit[v] >> (2 * j)) & 3) << (3 * j));
+        t->dig3[v] = d;
     }
-    for (int v = 0; v < 128; ++v) {
-        uint32_t ql = 0;
-        for (int j = 0; j < 3; ++j) ql |= ((t->quint[v] >> (3 * j)) & 7u) << (8 * j);
-        t->qlut[v] = ql;
-        // low half of a b=1 trit group: bit0 m0, bit1 T0, bit2 T1, bit3 m1, bit4 T2, bit5 T3, bit6 m2
-        uint64_t lo = 0;
-        lo |= static_cast<uint64_t>(v & 1) | (static_cast<uint64_t>((v >> 3) & 1) << 8) | (static_cast<uint64_t>((v >> 6) & 1) << 16);
-        const uint64_t tlo = ((v >> 1) & 3) | (((v >> 4) & 3) << 2);
-        t->t13lo[v] = lo | (tlo << 56);
-    }
-    for (int v = 0; v < 64; ++v) {
-        // high half: bit0 T4, bit1 m3, bit2 T5, bit3 T6, bit4 m4, bit5 T7
-        const uint64_t m = (static_cast<uint64_t>((v >> 1) & 1) << 24) | (static_cast<uint64_t>((v >> 4) & 1) << 32);
-        const uint64_t th = (v & 1) | (((v >> 2) & 3) << 1) | (((v >> 5) & 1) << 3);
-        t->t13hi[v] = m | (th << 60);
-    }
+    for (int v = 0; v < 128; ++v) t->dig3[256 + v] = t->quint[v];
     static const int kBlocks[kNumFootprints] = {4, 6, 8};
     for (int f = 0; f < kNumFootprints; ++f) {
         const int bs = kBlocks[f];

@@ -45,16 +45,9 @@ struct Tables {
     uint8_t cquant[10][128];                    // 0xFF: no range fits (illegal block)
     // Range shape per range index: bits | trits << 4 | quints << 5.
     uint8_t shape[21];
-    // Byte-spread tables for the SWAR weight decoders (one byte per value):
-    uint32_t spread2[256];   // four 2-bit fields -> 4 bytes
-    uint64_t spread1[256];   // eight bits -> 8 bytes
-    uint64_t tlut[256];      // 8-bit trit block -> 5 digit bytes
-    uint32_t qlut[128];      // 7-bit quint block -> 3 digit bytes
-    // Trit groups with one low bit per value (13 bits: m0 T0 T1 m1 T2 T3 m2 |
-    // T4 m3 T5 T6 m4 T7): low 7 bits -> m0..m2 in bytes 0..2, T0..T3 in bits
-    // 56..59; high 6 bits -> m3, m4 in bytes 3, 4, T4..T7 in bits 60..63.
-    uint64_t t13lo[128];
-    uint64_t t13hi[64];
+    // Digits of a trit block (index 0..255) or quint block (256 + 0..127),
+    // 3 bits per digit: the runtime BISE decoder's single lookup.
+    uint16_t dig3[384];
 };
 
 // Fills `t` on the host. Deterministic; no device calls.

@@ -60,38 +60,54 @@ extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, u
 
 extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 
-// The fast per-block path of the attention kernel's plane decode: sort key,
-// then (fast keys) value table + per-texel index bytes, or (constant keys)
-// the block's single value. Returns the fp16-view values of the R channel
-// per texel, or -1 for blocks that take the per-texel path; `cls` gets the key.
+// The per-block runtime path of the attention kernel's plane decode
+// (akv_decode_fast.cuh): block kind, then table / constant blocks (value table
+// + weight codes, read back as the kernel's tile writer reads them) or
+// descriptor blocks (evaluated per texel as the kernel's phase 1b does).
+// Returns the fp16-view values of the R channel per texel, or -1 for blocks
+// that take the generic path; `cls` gets the kind.
+template <int BS>
+static int fast_r_one(uint4 b, int* kind_out, float* out) {
+    namespace F = akv::fast;
+    constexpr int N = BS * BS;
+    uint32_t me;
+    int cq;
+    const int kind = F::block_kind<BS>(b, me, cq);
+    *kind_out = kind;
+    if (kind == F::kKindGeneric) { for (int t = 0; t < N; ++t) out[t] = -1.f; return 0; }
+    uint32_t tab[F::kTabCap];
+    uint8_t codes[64];
+    std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
+    akv::BlockDesc<1> d;
+    uint8_t w[64];
+    std::memset(w, 0, sizeof(w));
+    F::LumOut o;
+    F::decode_lum<BS>(b, kind, me, cq, false, 0.f, 0.f, tab, codes, 1, kind == F::kKindDesc ? &d : nullptr, w, o);
+    for (int t = 0; t < N; ++t) {
+        if (kind == F::kKindDesc) {
+            uint32_t cv[1];
+            akv::texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
+            out[t] = akv::c16_to_unit(cv[0]);
+        } else {
+            const uint32_t c = codes[t] & o.cmask;
+            const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
+            if (part * o.L + c >= static_cast<uint32_t>(F::kTabCap)) return 3;
+            out[t] = F::lum_unit(o, tab, codes, 1, t);
+        }
+    }
+    return 0;
+}
+
 extern "C" int emu_decode_fast_r(const uint8_t* blocks, int64_t n, int bs, float* out, int* cls) {
     static bool ready = false;
     if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
-    namespace F = akv::fast;
     for (int64_t i = 0; i < n; ++i) {
         uint4 b;
         std::memcpy(&b, blocks + 16 * i, 16);
-        const int c = bs == 4 ? F::block_key<4>(b) : bs == 6 ? F::block_key<6>(b) : F::block_key<8>(b);
-        cls[i] = c;
-        const int N = bs * bs;
-        if (c == F::kKeySlow) { for (int t = 0; t < N; ++t) out[i * N + t] = -1.f; continue; }
-        if (c == F::kKeyConst) {
-            const float u = akv::c16_to_unit(F::const_c16(b));
-            for (int t = 0; t < N; ++t) out[i * N + t] = u;
-            continue;
-        }
-        uint32_t tab[F::kTabCap];
-        uint32_t words[16];
-        int L = 0;
-        if (bs == 4) { F::Idx<4> ix; L = F::decode_fast_any<4>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
-        else if (bs == 6) { F::Idx<6> ix; L = F::decode_fast_any<6>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
-        else { F::Idx<8> ix; L = F::decode_fast_any<8>(c - F::kKeyFast, b, false, 0.f, 0.f, tab, 1, ix); std::memcpy(words, ix.w, sizeof(ix.w)); }
-        if (L == 0) return 2;
-        for (int t = 0; t < N; ++t) {
-            const uint32_t k = (words[t >> 2] >> (8 * (t & 3))) & 0xFF;
-            if (k >= static_cast<uint32_t>(F::kTabCap)) return 3;
-            out[i * N + t] = __uint_as_float(tab[k]);
-        }
+        const int rc = bs == 4 ? fast_r_one<4>(b, cls + i, out + i * 16)
+                     : bs == 6 ? fast_r_one<6>(b, cls + i, out + i * 36)
+                               : fast_r_one<8>(b, cls + i, out + i * 64);
+        if (rc) return rc;
     }
     return 0;
 }

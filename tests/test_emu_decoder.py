@@ -64,10 +64,11 @@ def emu_fast_r(blocks, bs):
 @pytest.mark.parametrize("source", ["golden", "random", "garbage", "encoder"])
 @pytest.mark.parametrize("bs", [4, 6, 8])
 def test_fast_table_decode_matches_oracle(source, bs):
-    """The attention kernel's per-block value-table decode (fast keys: single
-    weight plane, full-resolution grid, luminance-direct endpoints) and its
-    constant blocks (void extent, illegal encodings) against the oracle's fp16
-    view."""
+    """The attention kernel's runtime block decode against the oracle's fp16
+    view: table blocks (single weight plane, full-resolution grid,
+    luminance-direct endpoints), descriptor blocks (the same with a reduced
+    grid or a large table, evaluated per texel) and constant blocks (void
+    extent, illegal encodings)."""
     from astc_kv_cuda.ops import host_encode, random_blocks
     if source == "golden":
         if bs != 6:
@@ -84,8 +85,8 @@ def test_fast_table_decode_matches_oracle(source, bs):
         blocks = np.frombuffer(host_encode(x, bs, "scalar", 1), np.uint8).reshape(-1, 16)
     got, cls = emu_fast_r(blocks, bs)
     ref = O.decode_blocks(blocks, bs, O.OUT_FP16, threads=4)[..., 0].reshape(len(got), bs * bs).astype(np.float32)
-    table = cls != 1  # fast (value table) and constant blocks; key 1 takes the per-texel path
-    # Uniformly random bytes almost never form a fast block (valid full-grid
-    # mode and all-zero endpoint-mode fields); they exercise the constants.
-    assert (cls >= 2).any() if source != "garbage" else (cls == 0).any()
-    np.testing.assert_array_equal(got[table], ref[table])
+    covered = cls != 2  # every kind but the generic one (kKindGeneric = 2)
+    # Uniformly random bytes almost never form a luminance block (valid mode
+    # and all-zero endpoint-mode fields); they exercise the constants.
+    assert (cls <= 1).any() if source != "garbage" else (cls == 3).any()
+    np.testing.assert_array_equal(got[covered], ref[covered])
