@@ -196,11 +196,13 @@ struct DecodeScratch {
 };
 
 // Texels of one table / constant block -> the hi/lo tiles (pairs of columns
-// per 32-bit store). Rows at or past `rows` are written as zeros.
+// per 32-bit store), from the value table or, for kDirect footprints, from
+// endpoints and weights. Rows at or past `rows` are written as zeros.
 template <int BS, int LD>
 __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt,
-                                            int norm, const __half* moff, const __half* mscl, int row0, int col0,
-                                            int rows, int cols, __half (*thi)[LD], __half (*tlo)[LD]) {
+                                            int norm, float sc, float of, const __half* moff, const __half* mscl,
+                                            int row0, int col0, int rows, int cols, __half (*thi)[LD],
+                                            __half (*tlo)[LD]) {
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
     const uint32_t L = static_cast<uint32_t>(o.L);
 #pragma unroll
@@ -215,11 +217,26 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
         for (int x = 0; x < BS; x += 2) {
             if (x < cols) {
                 const int i = y * BS + x;
+                uint32_t h, l;
+                if constexpr (kDirect<BS>) {
+                    // Values from endpoints and weights (no table).
+                    const float u0 = direct_unit(o, codes, nt, i), u1 = direct_unit(o, codes, nt, i + 1);
+                    float s0 = sc, o0 = of, s1 = sc, o1 = of;
+                    if (norm == AKV_NORM_TOKEN) { s0 = s1 = rs; o0 = o1 = ro; }
+                    if (norm == AKV_NORM_PAGE_CHANNEL) {
+                        s0 = __half2float(mscl[col0 + x]); o0 = __half2float(moff[col0 + x]);
+                        s1 = __half2float(mscl[col0 + x + 1]); o1 = __half2float(moff[col0 + x + 1]);
+                    }
+                    split_pair(fmaf(u0, s0, o0), fmaf(u1, s1, o1), h, l);
+                    if (!rok) { h = 0u; l = 0u; }
+                    *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
+                    *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
+                    continue;
+                }
                 const uint32_t c0 = codes[i * nt] & o.cmask, c1 = codes[(i + 1) * nt] & o.cmask;
                 const uint32_t p0 = (o.pat[i >> 4] >> (2 * (i & 15))) & 3u;
                 const uint32_t p1 = (o.pat[(i + 1) >> 4] >> (2 * ((i + 1) & 15))) & 3u;
                 const uint32_t a = tab[(p0 * L + c0) * nt], b2 = tab[(p1 * L + c1) * nt];
-                uint32_t h, l;
                 if (affine) {
                     h = __byte_perm(a, b2, 0x5410);
                     l = __byte_perm(a, b2, 0x7632);
@@ -291,8 +308,8 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
         decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], THREADS,
                        slot >= 0 ? &ds.desc[slot] : nullptr, slot >= 0 ? ds.w[slot] : nullptr, o);
         if (slot < 0)
-            write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], THREADS, norm, moff, mscl, row0, col0, rows, ncol,
-                                thi, tlo);
+            write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], THREADS, norm, sc, of, moff, mscl, row0, col0,
+                                rows, ncol, thi, tlo);
     }
     __syncthreads();
     const int nslow = min(ds.nslot, kCap);

@@ -25,6 +25,12 @@ constexpr int kTabCap = 24;
 // Block kinds of the runtime path.
 enum : int { kKindTable = 0, kKindDesc = 1, kKindGeneric = 2, kKindConst = 3 };
 
+// Footprints whose table-kind blocks skip the value table: each texel's value
+// is computed from its endpoints and weight directly (a 4x4 block has 16
+// texels, fewer than most of its tables would have entries).
+template <int BS>
+constexpr bool kDirect = BS == 4;
+
 __device__ __forceinline__ int range_levels(int q) {
     const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
     return (1 << (shp & 15)) * (((shp >> 4) & 1) ? 3 : (((shp >> 5) & 1) ? 5 : 1));
@@ -128,7 +134,10 @@ __device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
     const int avail = 128 - mode_wbits(me) - (parts == 1 ? 17 : 29);
     cq = avail < 0 ? 0xFF : __ldg(&g_akv_tables.cquant[parts][avail]);
     if (cq == 0xFF) return kKindConst;
-    if ((me & kModeReduced) || parts * range_levels(mode_wq(me)) > kTabCap) return kKindDesc;
+    if (me & kModeReduced) return kKindDesc;
+    // 4x4 blocks are evaluated per texel in the thread (kDirect), so their
+    // table size does not matter.
+    if (!kDirect<BS> && parts * range_levels(mode_wq(me)) > kTabCap) return kKindDesc;
     return kKindTable;
 }
 
@@ -224,7 +233,27 @@ struct LumOut {
     uint32_t pat[4];  // partition per texel, 2 bits each
     int L;            // table entries per partition
     uint32_t cmask;   // 0xFF, or 0 for a constant block (every texel -> entry 0)
+    // Direct evaluation (kDirect footprints): endpoints of partitions 0..3
+    // as bytes, the weight unquantisation row, the constant's unit value.
+    uint32_t e0p, e1p;
+    const uint8_t* wun;
+    float cu;
 };
+
+// Unit value u (exact fp16 view as float) of a texel with 8-bit endpoints
+// e0, e1 and weight w (0..64).
+__device__ __forceinline__ float lerp_unit(uint32_t e0, uint32_t e1, uint32_t w) {
+    const uint32_t c = (257u * (e0 * (64u - w) + e1 * w) + 32u) >> 6;
+    return __int_as_float(__float_as_int(static_cast<float>(c + (c == 0xFFFFu))) & 0xFFFFE000) * 0x1p-16f;
+}
+
+// Unit value of texel t of a directly evaluated block.
+__device__ __forceinline__ float direct_unit(const LumOut& o, const uint8_t* codes, int nt, int t) {
+    if (!o.cmask) return o.cu;
+    const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
+    const uint32_t w = __ldg(o.wun + codes[t * nt]);
+    return lerp_unit((o.e0p >> (8 * part)) & 0xFFu, (o.e1p >> (8 * part)) & 0xFFu, w);
+}
 
 // Runtime path for table, descriptor and constant blocks (kind from
 // block_kind). Table / constant: tab and codes filled, `o` describes them.
@@ -245,10 +274,14 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
     const int L = lum ? range_levels(wq) : 1;
     o.L = L;
     o.cmask = lum ? 0xFFu : 0u;
+    o.wun = T.wunq[wq];
+    o.e0p = o.e1p = 0u;
+    o.cu = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) o.pat[k] = 0u;
     if (!lum) {
-        tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+        if constexpr (kDirect<BS>) o.cu = c16_to_unit(const_c16(blk));
+        else tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
         return;
     }
     int v[8];
@@ -259,7 +292,12 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
         mask_u128(clo, chi, bise_stream_bits_dev(2 * parts, cq));
         colors8(clo, chi, cq, v);
     }
-    if (kind == kKindTable) build_table(v, parts, wq, L, affine, sc, of, tab, nt);
+    if constexpr (kDirect<BS>) {
+        o.e0p = static_cast<uint32_t>(v[0] | (v[2] << 8) | (v[4] << 16) | (v[6] << 24));
+        o.e1p = static_cast<uint32_t>(v[1] | (v[3] << 8) | (v[5] << 16) | (v[7] << 24));
+    } else {
+        if (kind == kKindTable) build_table(v, parts, wq, L, affine, sc, of, tab, nt);
+    }
     if (parts > 1) {
         const uint32_t* pt = T.part[fp][parts - 2][(lo >> 13) & 0x3FF];
 #pragma unroll

@@ -62,7 +62,8 @@ extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 
 // The per-block runtime path of the attention kernel's plane decode
 // (akv_decode_fast.cuh): block kind, then table / constant blocks (value table
-// + weight codes, read back as the kernel's tile writer reads them) or
+// + weight codes, or per-texel endpoint/weight evaluation for 4x4, read back as
+// the kernel's tile writer reads them) or
 // descriptor blocks (evaluated per texel as the kernel's phase 1b does).
 // Returns the fp16-view values of the R channel per texel, or -1 for blocks
 // that take the generic path; `cls` gets the kind.
@@ -88,6 +89,8 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
             uint32_t cv[1];
             akv::texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
             out[t] = akv::c16_to_unit(cv[0]);
+        } else if constexpr (F::kDirect<BS>) {
+            out[t] = F::direct_unit(o, codes, 1, t);
         } else {
             const uint32_t c = codes[t] & o.cmask;
             const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
