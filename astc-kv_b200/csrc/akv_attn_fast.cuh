@@ -188,7 +188,7 @@ template <int NB, int NT, int N>
 struct DecodeScratch {
     static constexpr int kSlowCap = NB < 32 ? NB : 32;
     uint32_t tab[kTabCap][NT];  // value tables, thread-interleaved (conflict-free lookups)
-    uint8_t codes[N][NT];       // weight codes, thread-interleaved
+    uint8_t codes[N + kCodePad][NT];  // weight codes, thread-interleaved (+ slack rows)
     int nslot;                  // descriptor slots taken in this plane-chunk
     uint16_t slow_blk[kSlowCap];
     BlockDesc<1> desc[kSlowCap];

@@ -47,19 +47,22 @@ __device__ __forceinline__ uint32_t table_entry(float u, bool affine, float sc, 
     return static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
 }
 
-// Up to eight colour integers of range `cq` from a colour stream that starts
-// at bit 0 of (clo, chi) and is masked to its length, unquantised to 0..255
-// into registers (no local-memory arrays).
-__device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int (&v)[8]) {
+// The first nv (<= 8) colour integers of range `cq` from a colour stream
+// that starts at bit 0 of (clo, chi) and is masked to its length, unquantised
+// to 0..255 into registers (no local-memory arrays); v[nv..7] = 0.
+__device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int nv, int (&v)[8]) {
     const Tables& T = g_akv_tables;
     const uint32_t shp = __ldg(&T.shape[cq]);
     const int b = shp & 15;
     const uint64_t mm = (1ull << b) - 1ull;
     const uint8_t* un = T.cunq[cq];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0;
     if (shp & 0x10) {
         const int gb = 5 * b + 8;
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
+            if (5 * g >= nv) break;
             const uint64_t w = window_u128(clo, chi, g * gb);
             const uint32_t t = static_cast<uint32_t>((w >> b) & 3u) | static_cast<uint32_t>(((w >> (2 * b + 2)) & 3u) << 2) |
                                static_cast<uint32_t>(((w >> (3 * b + 4)) & 1u) << 4) |
@@ -70,7 +73,7 @@ __device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int 
 #pragma unroll
             for (int j = 0; j < 5; ++j) {
                 const int i = 5 * g + j;
-                if (i < 8) {
+                if (i < 8 && i < nv) {
                     const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
                     v[i] = __ldg(un + ((((dg >> (2 * j)) & 3u) << b) | m));
                 }
@@ -80,6 +83,7 @@ __device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int 
         const int gb = 3 * b + 7;
 #pragma unroll
         for (int g = 0; g < 3; ++g) {
+            if (3 * g >= nv) break;
             const uint64_t w = window_u128(clo, chi, g * gb);
             const uint32_t qv = static_cast<uint32_t>((w >> b) & 7u) | static_cast<uint32_t>(((w >> (2 * b + 3)) & 3u) << 3) |
                                 static_cast<uint32_t>(((w >> (3 * b + 5)) & 3u) << 5);
@@ -88,7 +92,7 @@ __device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int 
 #pragma unroll
             for (int j = 0; j < 3; ++j) {
                 const int i = 3 * g + j;
-                if (i < 8) {
+                if (i < 8 && i < nv) {
                     const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
                     v[i] = __ldg(un + ((((dg >> (3 * j)) & 7u) << b) | m));
                 }
@@ -96,7 +100,8 @@ __device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int 
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = __ldg(un + static_cast<uint32_t>(window_u128(clo, chi, i * b) & mm));
+        for (int i = 0; i < 8; ++i)
+            if (i < nv) v[i] = __ldg(un + static_cast<uint32_t>(window_u128(clo, chi, i * b) & mm));
     }
 }
 
@@ -145,7 +150,12 @@ __device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
 // stream (s0, s1), already masked to its length, into codes[i * nt]. Groups
 // of five (trits, plain bits) or three (quints) values per step, with the
 // trit/quint block bits gathered by runtime shifts and decoded through the
-// combined digit table.
+// combined digit table. Every step stores five codes without predicates: a
+// quint step's two extra codes are overwritten by the next step, and the
+// last step may write up to four rows past `count` (the caller provides
+// kCodePad rows of slack).
+constexpr int kCodePad = 4;
+
 __device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, int count, uint8_t* codes, int nt) {
     const Tables& T = g_akv_tables;
     const uint32_t shp = __ldg(&T.shape[wq]);
@@ -165,26 +175,29 @@ __device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, i
     const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
     const int o3 = 3 * b + (tr ? 5 : 0);
     const int o4 = 4 * b + (tr ? 7 : 0);
-    const int dbase = qu ? 256 : 0;
-    const uint32_t bm = (1u << b) - 1u;
+    const int b2 = 2 * b, b3 = 3 * b, b4 = 4 * b, b5 = 5 * b;
+    const uint16_t* dig = T.dig3 + (qu ? 256 : 0);
+    const uint32_t bm = (1u << b) - 1u, km = 7u << b;
+    // The stream as four 32-bit words, shifted down by `gb` per step.
+    uint32_t w0 = static_cast<uint32_t>(s0), w1 = static_cast<uint32_t>(s0 >> 32);
+    uint32_t w2 = static_cast<uint32_t>(s1), w3 = static_cast<uint32_t>(s1 >> 32);
     uint8_t* cp = codes;
-    int left = count;
+    const int step = gs * nt;
     for (int g = 0; g < ng; ++g) {
-        const uint32_t win = static_cast<uint32_t>(s0);
-        const uint32_t X = ((win >> b) & m1) | ((win >> (2 * b)) & m2) | ((win >> (3 * b)) & m3) |
-                           ((win >> (4 * b)) & m4) | ((win >> (5 * b)) & m5);
-        const uint32_t dg = __ldg(&T.dig3[dbase + X]);
-        cp[0] = static_cast<uint8_t>(((dg & 7u) << b) | (win & bm));
-        if (left > 1) cp[nt] = static_cast<uint8_t>((((dg >> 3) & 7u) << b) | ((win >> o1) & bm));
-        if (left > 2) cp[2 * nt] = static_cast<uint8_t>((((dg >> 6) & 7u) << b) | ((win >> o2) & bm));
-        if (!qu) {
-            if (left > 3) cp[3 * nt] = static_cast<uint8_t>((((dg >> 9) & 7u) << b) | ((win >> o3) & bm));
-            if (left > 4) cp[4 * nt] = static_cast<uint8_t>((((dg >> 12) & 7u) << b) | ((win >> o4) & bm));
-        }
-        cp += gs * nt;
-        left -= gs;
-        s0 = (s0 >> gb) | (s1 << (64 - gb));
-        s1 >>= gb;
+        const uint32_t win = w0;
+        const uint32_t X = ((win >> b) & m1) | ((win >> b2) & m2) | ((win >> b3) & m3) | ((win >> b4) & m4) |
+                           ((win >> b5) & m5);
+        const uint32_t dgb = static_cast<uint32_t>(__ldg(dig + X)) << b;
+        cp[0] = static_cast<uint8_t>((dgb & km) | (win & bm));
+        cp[nt] = static_cast<uint8_t>(((dgb >> 3) & km) | ((win >> o1) & bm));
+        cp[2 * nt] = static_cast<uint8_t>(((dgb >> 6) & km) | ((win >> o2) & bm));
+        cp[3 * nt] = static_cast<uint8_t>(((dgb >> 9) & km) | ((win >> o3) & bm));
+        cp[4 * nt] = static_cast<uint8_t>(((dgb >> 12) & km) | ((win >> o4) & bm));
+        cp += step;
+        w0 = __funnelshift_r(w0, w1, gb);
+        w1 = __funnelshift_r(w1, w2, gb);
+        w2 = __funnelshift_r(w2, w3, gb);
+        w3 >>= gb;
     }
 }
 
@@ -290,7 +303,7 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
         uint64_t clo = window_u128(lo, hi, cstart);
         uint64_t chi = hi >> cstart;
         mask_u128(clo, chi, bise_stream_bits_dev(2 * parts, cq));
-        colors8(clo, chi, cq, v);
+        colors8(clo, chi, cq, 2 * parts, v);
     }
     if constexpr (kDirect<BS>) {
         o.e0p = static_cast<uint32_t>(v[0] | (v[2] << 8) | (v[4] << 16) | (v[6] << 24));

@@ -19,6 +19,10 @@ inline unsigned long long __brevll(unsigned long long x) {
     for (int i = 0; i < 64; ++i) r |= ((x >> i) & 1ull) << (63 - i);
     return r;
 }
+inline unsigned __funnelshift_r(unsigned lo, unsigned hi, unsigned s) {
+    s &= 31;
+    return s ? (lo >> s) | (hi << (32 - s)) : lo;
+}
 inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
 inline int __float_as_int(float f) { int i; std::memcpy(&i, &f, 4); return i; }
 using std::max;
@@ -77,7 +81,7 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
     *kind_out = kind;
     if (kind == F::kKindGeneric) { for (int t = 0; t < N; ++t) out[t] = -1.f; return 0; }
     uint32_t tab[F::kTabCap];
-    uint8_t codes[64];
+    uint8_t codes[64 + akv::fast::kCodePad];
     std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
     akv::BlockDesc<1> d;
     uint8_t w[64];
