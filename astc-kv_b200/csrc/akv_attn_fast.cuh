@@ -184,11 +184,15 @@ __device__ __noinline__ void eval_block_generic(uint4 blk, int norm, float sc, f
 
 // Scratch of the decode of one plane-chunk of up to NB blocks by NT threads
 // (N = texels per block).
-template <int NB, int NT, int N>
+template <int NB, int NT, int BS>
 struct DecodeScratch {
+    static constexpr int N = BS * BS;
     static constexpr int kSlowCap = NB < 32 ? NB : 32;
-    uint32_t tab[kTabCap][NT];  // value tables, thread-interleaved (conflict-free lookups)
-    uint8_t codes[N + kCodePad][NT];  // weight codes, thread-interleaved (+ slack rows)
+    // Columns: one per decoding thread (a chunk with fewer blocks than
+    // threads leaves the others idle).
+    static constexpr int NC = NT < ((NB + 31) / 32) * 32 ? NT : ((NB + 31) / 32) * 32;
+    uint32_t tab[kTabCap<BS> > 0 ? kTabCap<BS> : 1][NC];  // value tables, thread-interleaved (conflict-free lookups)
+    uint8_t codes[N + kCodePad][NC];  // weight codes, thread-interleaved (+ slack rows)
     int nslot;                  // descriptor slots taken in this plane-chunk
     uint16_t slow_blk[kSlowCap];
     BlockDesc<1> desc[kSlowCap];
@@ -271,10 +275,10 @@ __device__ __forceinline__ void put_texel(float v, bool ok, int row, int col, __
 template <int BS, int D, int THREADS, int NB, int LD>
 __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* moff, const __half* mscl, int norm,
                                              int cols, int rows_blk, int n, bool valid,
-                                             DecodeScratch<NB, THREADS, BS * BS>& ds, __half (*thi)[LD],
+                                             DecodeScratch<NB, THREADS, BS>& ds, __half (*thi)[LD],
                                              __half (*tlo)[LD]) {
     constexpr int N = BS * BS;
-    constexpr int kCap = DecodeScratch<NB, THREADS, N>::kSlowCap;
+    constexpr int kCap = DecodeScratch<NB, THREADS, BS>::kSlowCap;
     const int nblk = rows_blk * cols;
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
     const int tid = threadIdx.x;
@@ -305,10 +309,11 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
             }
         }
         LumOut o;
-        decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], THREADS,
+        constexpr int NC = DecodeScratch<NB, THREADS, BS>::NC;
+        decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], NC,
                        slot >= 0 ? &ds.desc[slot] : nullptr, slot >= 0 ? ds.w[slot] : nullptr, o);
         if (slot < 0)
-            write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], THREADS, norm, sc, of, moff, mscl, row0, col0,
+            write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], NC, norm, sc, of, moff, mscl, row0, col0,
                                 rows, ncol, thi, tlo);
     }
     __syncthreads();
@@ -340,9 +345,11 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
 
 template <int D, int G, int VBS, int KBS>
 struct Cfg {
-    static constexpr int CH = (VBS == 6 || KBS == 6) ? 48 : 64;
+    // Tokens per chunk: 48 with a 6x6 plane; 32 with ASTC K (two decoded
+    // planes in shared memory); else 64.
+    static constexpr int CH = (VBS == 6 || KBS == 6) ? 48 : (KBS ? 32 : 64);
     static constexpr int NWM = CH / 16;                        // token tiles of 16 per chunk
-    static constexpr int THREADS = (VBS == 6) ? 192 : 256;
+    static constexpr int THREADS = 64 * NWM;                   // two warps per token tile
     static constexpr int LD = D + 8;                           // halves per tile row (16-byte pad)
     static constexpr int VCOLS = (D + VBS - 1) / VBS;
     static constexpr int VROWS = CH / VBS;
@@ -354,8 +361,8 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS * VBS>);
-    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 1) * (KBS ? KBS : 1)>) : 0;
+    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS>);
+    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
@@ -540,13 +547,13 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         // Decode V (and K) tiles.
         decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
                                                   CH / VBS, n, valid,
-                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS * VBS>*>(sm.ds), sm.vhi,
+                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds), sm.vhi,
                                                   sm.vlo);
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
             decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
-                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS, KB * KB>*>(sm.ds),
+                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS, KB>*>(sm.ds),
                                                 sm.khi, sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;

@@ -163,7 +163,7 @@ const FastVariant kFastVariants[] = {
 };
 #undef AKV_FAST
 
-int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : 64; }
+int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : (kbs ? 32 : 64); }
 
 const FastVariant* find_fast(int D, int G, int vbs, int kbs) {
     for (const FastVariant& v : kFastVariants)

@@ -8,7 +8,7 @@
 // stays small. A luminance-direct (endpoint mode 0), single-plane block with
 // a full-resolution grid becomes a value table (entry = partition * levels +
 // weight code, affine and fp16 hi/lo split folded in) plus one weight-code
-// byte per texel; with a reduced grid, or a table larger than kTabCap, it
+// byte per texel; with a reduced grid, or a table larger than kTabCap<BS>, it
 // becomes a descriptor evaluated per texel. Everything else takes the
 // generic decoder of akv_astc_device.cuh.
 #pragma once
@@ -19,8 +19,6 @@
 namespace akv {
 namespace fast {
 
-// Value-table capacity per block (entries = partitions * weight levels).
-constexpr int kTabCap = 24;
 
 // Block kinds of the runtime path.
 enum : int { kKindTable = 0, kKindDesc = 1, kKindGeneric = 2, kKindConst = 3 };
@@ -30,6 +28,13 @@ enum : int { kKindTable = 0, kKindDesc = 1, kKindGeneric = 2, kKindConst = 3 };
 // texels, fewer than most of its tables would have entries).
 template <int BS>
 constexpr bool kDirect = BS == 4;
+
+// Value-table capacity per block (entries = partitions * weight levels) by
+// footprint: none for directly evaluated 4x4 blocks; a full-resolution 8x8
+// grid only fits two weight levels (at most 8 entries).
+template <int BS>
+constexpr int kTabCap = BS == 4 ? 0 : (BS == 8 ? 8 : 24);
+constexpr int kTabCapMax = 24;
 
 __device__ __forceinline__ int range_levels(int q) {
     const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
@@ -142,7 +147,7 @@ __device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
     if (me & kModeReduced) return kKindDesc;
     // 4x4 blocks are evaluated per texel in the thread (kDirect), so their
     // table size does not matter.
-    if (!kDirect<BS> && parts * range_levels(mode_wq(me)) > kTabCap) return kKindDesc;
+    if (!kDirect<BS> && parts * range_levels(mode_wq(me)) > kTabCap<BS>) return kKindDesc;
     return kKindTable;
 }
 

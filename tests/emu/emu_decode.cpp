@@ -80,7 +80,7 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
     const int kind = F::block_kind<BS>(b, me, cq);
     *kind_out = kind;
     if (kind == F::kKindGeneric) { for (int t = 0; t < N; ++t) out[t] = -1.f; return 0; }
-    uint32_t tab[F::kTabCap];
+    uint32_t tab[F::kTabCapMax];
     uint8_t codes[64 + akv::fast::kCodePad];
     std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
     akv::BlockDesc<1> d;
@@ -98,7 +98,7 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
         } else {
             const uint32_t c = codes[t] & o.cmask;
             const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
-            if (part * o.L + c >= static_cast<uint32_t>(F::kTabCap)) return 3;
+            if (part * o.L + c >= static_cast<uint32_t>(F::kTabCap<BS>)) return 3;
             out[t] = F::lum_unit(o, tab, codes, 1, t);
         }
     }
