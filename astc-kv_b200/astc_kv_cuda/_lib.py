@@ -18,6 +18,7 @@ AKV_LAYOUT_SCALAR, AKV_LAYOUT_RGBA = 0, 1
 AKV_NORM_PAGE_CHANNEL, AKV_NORM_TOKEN, AKV_NORM_BLOCK_AFFINE = 0, 1, 2
 AKV_Q_F32, AKV_Q_BF16, AKV_Q_F16 = 0, 1, 2
 AKV_PHASE_SPLIT, AKV_PHASE_MERGE = 1, 2
+AKV_KERNEL_GENERIC, AKV_KERNEL_FAST = 0, 1
 AKV_ERR_STATIC_WORKSPACE = 8
 AKV_STATIC_WORKSPACE_BYTES = 8 << 20
 
@@ -53,7 +54,8 @@ class AkvAttnDesc(ct.Structure):
 # Every symbol include/akv_cuda.h and include/akv_host.h declare.
 EXPORTS = (
     "akv_cuda_error", "akv_cuda_abi_version", "akv_cuda_init", "akv_cuda_decode_blocks", "akv_cuda_decode_image",
-    "akv_cuda_attention_workspace", "akv_cuda_decode_attention", "akv_cuda_decode_attention_phase",
+    "akv_cuda_attention_workspace", "akv_cuda_attention_plan", "akv_cuda_decode_attention",
+    "akv_cuda_decode_attention_phase",
     "akv_cuda_decode_attention_noalloc", "akv_cuda_restore_plane", "akv_cuda_struct_size",
     "akv_cuda_host_tables", "akv_host_encode", "akv_host_random_blocks",
 )
@@ -91,6 +93,8 @@ def lib() -> ct.CDLL:
         l.akv_cuda_decode_image.argtypes = [vp, sz, ct.c_int, vp, ct.c_uint, ct.c_uint, vp]
         l.akv_cuda_attention_workspace.argtypes = [ct.POINTER(AkvAttnDesc)]
         l.akv_cuda_attention_workspace.restype = sz
+        ip = ct.POINTER(ct.c_int)
+        l.akv_cuda_attention_plan.argtypes = [ct.POINTER(AkvAttnDesc), ip, ip, ip]
         l.akv_cuda_decode_attention.argtypes = [ct.POINTER(AkvAttnDesc), vp]
         l.akv_cuda_decode_attention_phase.argtypes = [ct.POINTER(AkvAttnDesc), ct.c_int, vp]
         l.akv_cuda_decode_attention_noalloc.argtypes = [ct.POINTER(AkvAttnDesc), vp]

@@ -227,6 +227,13 @@ class Attention:
         L.check(L.lib().akv_cuda_decode_attention(self._dref, _stream_handle(stream)), "decode_attention")
         return self.out
 
+    def plan(self) -> dict:
+        """The launch plan (akv_cuda_attention_plan): kernel name, split size, splits."""
+        k, sp, ns = ct.c_int(), ct.c_int(), ct.c_int()
+        L.check(L.lib().akv_cuda_attention_plan(self._dref, ct.byref(k), ct.byref(sp), ct.byref(ns)), "attention_plan")
+        return {"kernel": "attn_fast_kernel" if k.value == L.AKV_KERNEL_FAST else "attn_split_kernel",
+                "split_tokens": sp.value, "nsplits": ns.value}
+
     def run_phase(self, phase: int, stream: torch.cuda.Stream | None = None) -> None:
         """Issue only the split (1) or merge (2) launch; see akv_cuda_decode_attention_phase."""
         L.check(L.lib().akv_cuda_decode_attention_phase(self._dref, phase, _stream_handle(stream)), "decode_attention")

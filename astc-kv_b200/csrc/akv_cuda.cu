@@ -430,6 +430,15 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc) {
     return plan_attention(desc, &plan) == AKV_OK ? plan.ws : 0;
 }
 
+int akv_cuda_attention_plan(const AkvAttnDesc* desc, int* kernel, int* split_tokens, int* nsplits) {
+    AttnPlan plan;
+    if (int st = plan_attention(desc, &plan)) return st;
+    if (kernel) *kernel = plan.fast ? AKV_KERNEL_FAST : AKV_KERNEL_GENERIC;
+    if (split_tokens) *split_tokens = plan.split;
+    if (nsplits) *nsplits = plan.nsplits;
+    return AKV_OK;
+}
+
 int akv_cuda_decode_attention(const AkvAttnDesc* d, void* stream) {
     return akv_cuda_decode_attention_phase(d, AKV_PHASE_SPLIT | AKV_PHASE_MERGE, stream);
 }

@@ -459,7 +459,7 @@ def run_ours(args) -> dict | None:
                    "l2": "inputs larger than L2 (no flush needed)", "bytes_per_step_per_gpu": wl.bytes},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": hbm_src + " (MEASURED_PEAKS.json hbm_gbs)" if hbm_src == "measured" else hbm_src,
-                     "kernel": "attn_split_kernel", "kernel_ms": split_ms,
+                     "kernel": wl.attn.plan()["kernel"], "kernel_ms": split_ms,
                      "traffic": TRAFFIC.get(args.workload)},
         "e2e": {"value": toks / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": wl.q.numel() * wl.q.element_size(),
@@ -474,8 +474,11 @@ def run_ours(args) -> dict | None:
     return line
 
 
-# Per-launch DRAM traffic from the committed ncu captures (profiles/), bytes.
-TRAFFIC: dict[str, float | None] = {}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
+# the split kernel from the committed ncu captures (profiles/), bytes: c2 was
+# captured at batch 4 (352.1 MB) and scaled by the 8x units of the batch-32
+# launch (traffic grows with the batch).
+TRAFFIC: dict[str, float | None] = {"c2": 352.116e6 * 8}
 
 
 # ------------------------------------------------------------- CPU reference path

@@ -149,6 +149,17 @@ typedef struct AkvAttnDesc {
 /* Workspace bytes the descriptor needs (0 on invalid descriptors). */
 size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc);
 
+/* The launch plan of a descriptor, without launching: which split kernel
+ * runs (AKV_KERNEL_FAST: fused decode + tensor-core kernel for scalar ASTC V
+ * with whole chunks per page and 16-byte aligned metadata; AKV_KERNEL_GENERIC
+ * otherwise), the split size in tokens and the number of splits. Any output
+ * pointer may be NULL. Returns the status akv_cuda_decode_attention would
+ * return for a descriptor error. No counterpart in the reference (its Metal
+ * host picks kernels in the probe programs). */
+#define AKV_KERNEL_GENERIC 0
+#define AKV_KERNEL_FAST 1
+int akv_cuda_attention_plan(const AkvAttnDesc* desc, int* kernel, int* split_tokens, int* nsplits);
+
 int akv_cuda_decode_attention(const AkvAttnDesc* desc, void* stream);
 
 /* The two launches of akv_cuda_decode_attention issued one at a time, so a

@@ -77,6 +77,10 @@ def test_attention_descriptor_validation():
     d.v.data, d.v.offsets, d.v.scales = 8192, 8192, 8192
     ws = lib.akv_cuda_attention_workspace(ct.byref(d))
     assert ws > 0
+    kern, split, nsplits = ct.c_int(-1), ct.c_int(0), ct.c_int(0)
+    assert lib.akv_cuda_attention_plan(ct.byref(d), ct.byref(kern), ct.byref(split), ct.byref(nsplits)) == 0
+    assert kern.value in (L.AKV_KERNEL_GENERIC, L.AKV_KERNEL_FAST)
+    assert split.value % 6 == 0 and nsplits.value == -(-384 // split.value)
     # Missing workspace -> AKV_ERR_WORKSPACE before any launch.
     d.q_dev, d.out_dev = 4096, 4096
     assert lib.akv_cuda_decode_attention(ct.byref(d), None) == 6
