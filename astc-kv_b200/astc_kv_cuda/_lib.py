@@ -54,7 +54,8 @@ class AkvAttnDesc(ct.Structure):
 # Every symbol include/akv_cuda.h and include/akv_host.h declare.
 EXPORTS = (
     "akv_cuda_error", "akv_cuda_abi_version", "akv_cuda_init", "akv_cuda_decode_blocks", "akv_cuda_decode_image",
-    "akv_cuda_attention_workspace", "akv_cuda_attention_plan", "akv_cuda_decode_attention",
+    "akv_cuda_attention_workspace", "akv_cuda_attention_plan", "akv_cuda_attention_tail_workspace",
+    "akv_cuda_decode_attention_tail", "akv_cuda_decode_attention",
     "akv_cuda_decode_attention_phase",
     "akv_cuda_decode_attention_noalloc", "akv_cuda_restore_plane", "akv_cuda_struct_size",
     "akv_cuda_host_tables", "akv_host_encode", "akv_host_random_blocks",
@@ -95,6 +96,9 @@ def lib() -> ct.CDLL:
         l.akv_cuda_attention_workspace.restype = sz
         ip = ct.POINTER(ct.c_int)
         l.akv_cuda_attention_plan.argtypes = [ct.POINTER(AkvAttnDesc), ip, ip, ip]
+        l.akv_cuda_attention_tail_workspace.argtypes = [ct.POINTER(AkvAttnDesc), ct.POINTER(AkvAttnDesc)]
+        l.akv_cuda_attention_tail_workspace.restype = sz
+        l.akv_cuda_decode_attention_tail.argtypes = [ct.POINTER(AkvAttnDesc), ct.POINTER(AkvAttnDesc), vp]
         l.akv_cuda_decode_attention.argtypes = [ct.POINTER(AkvAttnDesc), vp]
         l.akv_cuda_decode_attention_phase.argtypes = [ct.POINTER(AkvAttnDesc), ct.c_int, vp]
         l.akv_cuda_decode_attention_noalloc.argtypes = [ct.POINTER(AkvAttnDesc), vp]

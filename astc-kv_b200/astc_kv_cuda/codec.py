@@ -317,12 +317,17 @@ def encode_tensor(x: np.ndarray, config: dict, page_tokens: int = 96, quality: f
                          p_tokens if permutation else None, p_channels if permutation else None)
 
 
-def attention(q, k, v, positions):
+def attention(q, k, v, positions, k_tail=None, v_tail=None):
     """GQA causal attention with the reference's signature (codec.py:253-267).
 
     ``k`` and ``v`` are ``EncodedTensor`` (ASTC planes read directly by the
     kernel) or fp16-representable arrays ``[Hkv, T, D]`` (fp16 planes). Query
     i attends tokens t <= positions[i]. Returns ``(out [Hq, N, D], None)``.
+
+    ``k_tail`` / ``v_tail`` (optional, arrays ``[Hkv, n, D]``, kept in FP16):
+    the newest tokens that do not fill a page yet, positions T .. T + n - 1 of
+    the same sequence, attended in the same softmax (the reference's encoder
+    rejects incomplete pages, codec.py:132-133).
     """
     import torch
     from .ops import Attention, contiguous_fp16_plane
@@ -354,8 +359,21 @@ def attention(q, k, v, positions):
         p.meta_stride_batch = 0
         p.side_stride_batch = 0
     qd = torch.from_numpy(np.ascontiguousarray(q.transpose(1, 0, 2))).cuda()
-    lens = torch.from_numpy(np.asarray(positions, np.int64) + 1).clamp(0, tk).to(torch.int32).cuda()
-    out = Attention(qd, kp, vp, page_tokens=page, max_tokens=tk, seq_lens=lens).run()
+    pos1 = np.asarray(positions, np.int64) + 1
+    lens = torch.from_numpy(pos1).clamp(0, tk).to(torch.int32).cuda()
+    tail = {}
+    if (k_tail is None) != (v_tail is None):
+        raise ValueError("k_tail and v_tail go together")
+    if k_tail is not None:
+        tkp, htk, ntk, _ = plane(k_tail)
+        tvp, htv, ntv, _ = plane(v_tail)
+        if (htk, ntk) != (htv, ntv) or htk != hk:
+            raise ValueError("Incompatible attention shapes")
+        for p in (tkp, tvp):
+            p.stride_batch = 0
+        tail = {"tail_k": tkp, "tail_v": tvp, "tail_tokens": ntk,
+                "tail_lens": torch.from_numpy(pos1 - tk).clamp(0, ntk).to(torch.int32).cuda()}
+    out = Attention(qd, kp, vp, page_tokens=page, max_tokens=tk, seq_lens=lens, **tail).run()
     return out.cpu().numpy().transpose(1, 0, 2).copy(), None
 
 

@@ -163,48 +163,79 @@ def paged_fp16_plane(pages: torch.Tensor) -> DevicePlane:
 _Q_DTYPES = {torch.float32: L.AKV_Q_F32, torch.bfloat16: L.AKV_Q_BF16, torch.float16: L.AKV_Q_F16}
 
 
+def _segment_desc(q: torch.Tensor, k: DevicePlane, v: DevicePlane, max_tokens: int, page_tokens: int,
+                  seq_lens: torch.Tensor | None, block_table: torch.Tensor | None, num_pages: int,
+                  split_tokens: int, keep: list) -> L.AkvAttnDesc:
+    """Descriptor of one KV segment for query q [B, Hq, D] (no io pointers)."""
+    B, Hq, D = q.shape
+    d = L.AkvAttnDesc()
+    d.batch, d.q_heads, d.head_dim = B, Hq, D
+    d.kv_heads = Attention._kv_heads(k, v, Hq)
+    for pl in (k, v):
+        if block_table is None and pl.capacity_tokens and max_tokens > pl.capacity_tokens:
+            raise ValueError("max_tokens exceeds the tokens the contiguous plane holds")
+        if block_table is None and not pl.capacity_tokens:
+            raise ValueError("a paged plane needs a block table")
+        if block_table is not None and pl.capacity_tokens and pl.stride_batch:
+            raise ValueError("a contiguous plane cannot be addressed through a block table")
+    d.max_tokens, d.page_tokens, d.split_tokens = max_tokens, page_tokens, split_tokens
+    lens = seq_lens.to(torch.int32).contiguous() if seq_lens is not None else None
+    table = block_table.to(torch.int32).contiguous() if block_table is not None else None
+    keep += [lens, table]
+    d.seq_lens_dev = _ptr(lens)
+    d.block_table_dev = _ptr(table)
+    if table is not None:
+        d.pages_per_seq = int(table.shape[1])
+        d.num_pages = int(num_pages)
+    d.k, d.v = k.to_c(), v.to_c()
+    return d
+
+
 class Attention:
     """A prepared decode-attention call (descriptor, workspace, output).
 
     Building the descriptor once and re-issuing `run()` keeps the per-step
     host cost to one C call; `run()` is what the benchmark times.
+
+    An optional second KV segment (`tail_k`, `tail_v`: planes of, e.g., the
+    exact FP16 tokens of each sequence's incomplete last page, `tail_lens`
+    tokens per sequence out of `tail_tokens`) is attended in the same softmax
+    through akv_cuda_decode_attention_tail.
     """
 
     def __init__(self, q: torch.Tensor, k: DevicePlane, v: DevicePlane, *, page_tokens: int, max_tokens: int,
                  seq_lens: torch.Tensor | None = None, block_table: torch.Tensor | None = None,
                  num_pages: int = 0, split_tokens: int = 0, scale: float = 0.0, out: torch.Tensor | None = None,
-                 status: torch.Tensor | None = None):
+                 status: torch.Tensor | None = None, tail_k: DevicePlane | None = None,
+                 tail_v: DevicePlane | None = None, tail_lens: torch.Tensor | None = None, tail_tokens: int = 0):
         _require_cuda(q, k.data, v.data, seq_lens, block_table)
         B, Hq, D = q.shape
         self.q, self.k, self.v = q, k, v
-        d = L.AkvAttnDesc()
-        d.batch, d.q_heads, d.head_dim = B, Hq, D
-        d.kv_heads = self._kv_heads(k, v, Hq)
-        for pl in (k, v):
-            if block_table is None and pl.capacity_tokens and max_tokens > pl.capacity_tokens:
-                raise ValueError("max_tokens exceeds the tokens the contiguous plane holds")
-            if block_table is None and not pl.capacity_tokens:
-                raise ValueError("a paged plane needs a block table")
-            if block_table is not None and pl.capacity_tokens and pl.stride_batch:
-                raise ValueError("a contiguous plane cannot be addressed through a block table")
-        d.max_tokens, d.page_tokens, d.split_tokens = max_tokens, page_tokens, split_tokens
+        self._keep: list = []
+        d = _segment_desc(q, k, v, max_tokens, page_tokens, seq_lens, block_table, num_pages, split_tokens, self._keep)
+        self.seq_lens, self.block_table = self._keep[0], self._keep[1]
         if q.dtype not in _Q_DTYPES or not q.is_contiguous():
             raise ValueError("q must be contiguous fp32/bf16/fp16 [B, Hq, D]")
         d.q_dtype = _Q_DTYPES[q.dtype]
         d.q_dev = q.data_ptr()
-        self.seq_lens = seq_lens.to(torch.int32).contiguous() if seq_lens is not None else None
-        self.block_table = block_table.to(torch.int32).contiguous() if block_table is not None else None
-        d.seq_lens_dev = _ptr(self.seq_lens)
-        d.block_table_dev = _ptr(self.block_table)
-        if self.block_table is not None:
-            d.pages_per_seq = int(self.block_table.shape[1])
-            d.num_pages = int(num_pages)
-        d.k, d.v = k.to_c(), v.to_c()
         d.scale = scale
-        ws = L.lib().akv_cuda_attention_workspace(ct.byref(d))
+        self.tail = None
+        if (tail_k is None) != (tail_v is None):
+            raise ValueError("a tail needs both K and V planes")
+        if tail_k is not None:
+            _require_cuda(tail_k.data, tail_v.data, tail_lens)
+            if tail_tokens <= 0:
+                raise ValueError("tail_tokens must be positive")
+            self.tail = _segment_desc(q, tail_k, tail_v, tail_tokens, tail_tokens, tail_lens, None, 0, 0, self._keep)
+            self._tref = ct.byref(self.tail)
+            ws = L.lib().akv_cuda_attention_tail_workspace(ct.byref(d), self._tref)
+        else:
+            ws = L.lib().akv_cuda_attention_workspace(ct.byref(d))
         if ws == 0:
             # Surface the precise validation error.
             d.workspace_dev, d.workspace_bytes = None, 0
+            if self.tail is not None:
+                L.check(L.lib().akv_cuda_decode_attention_tail(ct.byref(d), self._tref, None), "decode_attention_tail")
             L.check(L.lib().akv_cuda_decode_attention(ct.byref(d), None), "decode_attention")
         self.workspace = torch.empty(ws // 4 + 4, dtype=torch.float32, device=q.device)
         d.workspace_dev, d.workspace_bytes = self.workspace.data_ptr(), ws
@@ -224,7 +255,11 @@ class Attention:
         return int(k.kv_heads)
 
     def run(self, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-        L.check(L.lib().akv_cuda_decode_attention(self._dref, _stream_handle(stream)), "decode_attention")
+        if self.tail is not None:
+            L.check(L.lib().akv_cuda_decode_attention_tail(self._dref, self._tref, _stream_handle(stream)),
+                    "decode_attention_tail")
+        else:
+            L.check(L.lib().akv_cuda_decode_attention(self._dref, _stream_handle(stream)), "decode_attention")
         return self.out
 
     def plan(self) -> dict:
@@ -236,6 +271,8 @@ class Attention:
 
     def run_phase(self, phase: int, stream: torch.cuda.Stream | None = None) -> None:
         """Issue only the split (1) or merge (2) launch; see akv_cuda_decode_attention_phase."""
+        if self.tail is not None:
+            raise ValueError("phase-by-phase launches are not available with a tail segment")
         L.check(L.lib().akv_cuda_decode_attention_phase(self._dref, phase, _stream_handle(stream)), "decode_attention")
 
 

@@ -24,6 +24,11 @@ constexpr int kAttnThreads = 256;
 
 struct AttnParams {
     int B, Hq, Hkv, T, page_tokens, split_tokens, nsplits;
+    // Partials of split s of (b, query head hq) sit at row
+    // (b * Hq + hq) * split_stride + split_base + s of the workspace; the
+    // merge reads `split_stride` rows when merge_all is set (several KV
+    // segments share one workspace), else the rows the sequence length uses.
+    int split_base, split_stride, merge_all;
     int q_dtype;
     const void* q;
     const int32_t* seq_lens;
@@ -83,14 +88,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     const int len = seq_len_of(p, b);
     const int t_begin = split * p.split_tokens;
     const int t_end = min(t_begin + p.split_tokens, len);
-    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + h * G) * p.nsplits + split;  // + g * nsplits
+    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + h * G) * p.split_stride + p.split_base + split;  // + g * split_stride
 
     if (t_begin >= t_end) {
         for (int i = tid; i < G * D; i += kAttnThreads)
-            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.nsplits) * D + i % D] = 0.f;
+            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = 0.f;
         if (tid < G) {
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 0] = -CUDART_INF_F;
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 1] = 0.f;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 0] = -CUDART_INF_F;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 1] = 0.f;
         }
         return;
     }
@@ -252,11 +257,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < TG; ++k) s += red[k * G * D + i];
-        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.nsplits) * D + i % D] = s;
+        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = s;
     }
     if (tid < G) {
-        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 0] = m_s[tid];
-        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 1] = l_s[tid];
+        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 0] = m_s[tid];
+        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 1] = l_s[tid];
     }
 }
 
@@ -264,16 +269,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
 __global__ void merge_kernel(AttnParams p, int D) {
     const int hq = blockIdx.x, b = blockIdx.y;
     const int len = seq_len_of(p, b);
-    const int ns = min(p.nsplits, (len + p.split_tokens - 1) / p.split_tokens);
-    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + hq) * p.nsplits;
+    const int ns = p.merge_all ? p.split_stride : min(p.nsplits, (len + p.split_tokens - 1) / p.split_tokens);
+    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + hq) * p.split_stride;
     float M = -CUDART_INF_F;
     for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_ml[(unit0 + s) * 2]);
+    // Weight of split s; empty splits (m = -inf) weigh 0, also when every
+    // split is empty (M = -inf), so nothing to attend gives zeros.
+    auto weight = [&](int s) {
+        const float m = p.part_ml[(unit0 + s) * 2];
+        return m == -CUDART_INF_F ? 0.f : exp2f(m - M);
+    };
     float den = 0.f;
-    for (int s = 0; s < ns; ++s) den += exp2f(p.part_ml[(unit0 + s) * 2] - M) * p.part_ml[(unit0 + s) * 2 + 1];
+    for (int s = 0; s < ns; ++s) den += weight(s) * p.part_ml[(unit0 + s) * 2 + 1];
     const float inv = (ns > 0 && den > 0.f) ? 1.f / den : 0.f;
     for (int c = threadIdx.x; c < D; c += blockDim.x) {
         float num = 0.f;
-        for (int s = 0; s < ns; ++s) num += exp2f(p.part_ml[(unit0 + s) * 2] - M) * p.part_acc[(unit0 + s) * D + c];
+        for (int s = 0; s < ns; ++s) num += weight(s) * p.part_acc[(unit0 + s) * D + c];
         p.out[(static_cast<int64_t>(b) * p.Hq + hq) * D + c] = num * inv;
     }
 }

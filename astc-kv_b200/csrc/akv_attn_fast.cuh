@@ -404,13 +404,13 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
     const int len = seq_len_of(p, b);
     const int t_begin = split * p.split_tokens;
     const int t_end = min(t_begin + p.split_tokens, len);
-    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + h * G) * p.nsplits + split;
+    const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + h * G) * p.split_stride + p.split_base + split;
     if (t_begin >= t_end) {
         for (int i = tid; i < G * D; i += THREADS)
-            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.nsplits) * D + i % D] = 0.f;
+            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = 0.f;
         if (tid < G) {
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 0] = -CUDART_INF_F;
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 1] = 0.f;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 0] = -CUDART_INF_F;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 1] = 0.f;
         }
         return;
     }
@@ -702,10 +702,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
             mbar_wait(&sm.bar[0], 0);
         }
         for (int i = tid; i < G * D; i += THREADS)
-            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.nsplits) * D + i % D] = 0.f;
+            p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = 0.f;
         if (tid < G) {
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 0] = -CUDART_INF_F;
-            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 1] = 0.f;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 0] = -CUDART_INF_F;
+            p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 1] = 0.f;
         }
         return;
     }
@@ -745,7 +745,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
     }
     __syncthreads();
     for (int i = tid; i < G * D; i += THREADS)
-        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.nsplits) * D + i % D] = red[i];
+        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = red[i];
     if (tid < G) {
         float M = -CUDART_INF_F;
         for (int w = 0; w < NWM; ++w) M = fmaxf(M, sm.wm[w][tid]);
@@ -753,8 +753,8 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         if (M != -CUDART_INF_F)
             for (int w = 0; w < NWM; ++w)
                 if (sm.wm[w][tid] != -CUDART_INF_F) L += exp2f(sm.wm[w][tid] - M) * sm.wl[w][tid];
-        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 0] = M;
-        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.nsplits) * 2 + 1] = L;
+        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 0] = M;
+        p.part_ml[(unit0 + static_cast<int64_t>(tid) * p.split_stride) * 2 + 1] = L;
     }
 }
 

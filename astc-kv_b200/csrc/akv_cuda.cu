@@ -350,6 +350,42 @@ int launch_restore(const PlaneDev& pl, int B, int H, int T, int D, int P, const 
     return launch_status();
 }
 
+
+// Kernel parameters of one KV segment `d` (its planes, lengths and split
+// plan) writing split rows [split_base, split_base + plan.nsplits) of a
+// workspace with `stride` rows per (sequence, query head); query, output,
+// status and scale come from `io`.
+AttnParams segment_params(const AkvAttnDesc* d, const AttnPlan& plan, const AkvAttnDesc* io, int split_base,
+                          int stride) {
+    AttnParams p;
+    p.B = d->batch; p.Hq = d->q_heads; p.Hkv = d->kv_heads; p.T = d->max_tokens;
+    p.page_tokens = d->page_tokens; p.split_tokens = plan.split; p.nsplits = plan.nsplits;
+    p.split_base = split_base; p.split_stride = stride; p.merge_all = 0;
+    p.q_dtype = io->q_dtype; p.q = io->q_dev;
+    p.seq_lens = d->seq_lens_dev; p.table = d->block_table_dev;
+    p.pps = d->pages_per_seq; p.num_pages = d->num_pages;
+    p.k = to_dev(d->k); p.v = to_dev(d->v);
+    const float scale = io->scale > 0.f ? io->scale : 1.0f / std::sqrt(static_cast<float>(io->head_dim));
+    p.qscale = scale * 1.4426950408889634f;
+    float* ws = static_cast<float*>(io->workspace_dev);
+    p.part_acc = ws;
+    p.part_ml = ws + static_cast<size_t>(io->batch) * io->q_heads * stride * io->head_dim;
+    p.out = io->out_dev;
+    p.status = io->status_dev;
+    return p;
+}
+
+int launch_segment(const AkvAttnDesc* d, const AttnPlan& plan, const AttnParams& p, cudaStream_t s, int phase) {
+    if (plan.fast) return find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs)->fn(p, s, phase);
+    return find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl)->fn(p, s, phase);
+}
+
+// A tail descriptor must describe the same sequences and heads as the main one.
+bool tail_matches(const AkvAttnDesc* d, const AkvAttnDesc* t) {
+    return t && t->batch == d->batch && t->q_heads == d->q_heads && t->kv_heads == d->kv_heads &&
+           t->head_dim == d->head_dim;
+}
+
 }  // namespace
 }  // namespace akv
 
@@ -443,6 +479,7 @@ int akv_cuda_decode_attention(const AkvAttnDesc* d, void* stream) {
     return akv_cuda_decode_attention_phase(d, AKV_PHASE_SPLIT | AKV_PHASE_MERGE, stream);
 }
 
+
 int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* stream) {
     if (phase < AKV_PHASE_SPLIT || phase > (AKV_PHASE_SPLIT | AKV_PHASE_MERGE)) return AKV_ERR_INVALID_ARGUMENT;
     AttnPlan plan;
@@ -451,26 +488,35 @@ int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* strea
     if (!d->workspace_dev || d->workspace_bytes < plan.ws) return AKV_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(d->workspace_dev) % 16) return AKV_ERR_INVALID_ARGUMENT;
     if (int st = ensure_init()) return st;
-    AttnParams p;
-    p.B = d->batch; p.Hq = d->q_heads; p.Hkv = d->kv_heads; p.T = d->max_tokens;
-    p.page_tokens = d->page_tokens; p.split_tokens = plan.split; p.nsplits = plan.nsplits;
-    p.q_dtype = d->q_dtype; p.q = d->q_dev;
-    p.seq_lens = d->seq_lens_dev; p.table = d->block_table_dev;
-    p.pps = d->pages_per_seq; p.num_pages = d->num_pages;
-    p.k = to_dev(d->k); p.v = to_dev(d->v);
-    const float scale = d->scale > 0.f ? d->scale : 1.0f / std::sqrt(static_cast<float>(d->head_dim));
-    p.qscale = scale * 1.4426950408889634f;
-    float* ws = static_cast<float*>(d->workspace_dev);
-    p.part_acc = ws;
-    p.part_ml = ws + static_cast<size_t>(d->batch) * d->q_heads * plan.nsplits * d->head_dim;
-    p.out = d->out_dev;
-    p.status = d->status_dev;
-    if (plan.fast) {
-        const FastVariant* f = find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs);
-        return f->fn(p, static_cast<cudaStream_t>(stream), phase);
-    }
-    const Variant* v = find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl);
-    return v->fn(p, static_cast<cudaStream_t>(stream), phase);
+    const AttnParams p = segment_params(d, plan, d, 0, plan.nsplits);
+    return launch_segment(d, plan, p, static_cast<cudaStream_t>(stream), phase);
+}
+
+size_t akv_cuda_attention_tail_workspace(const AkvAttnDesc* desc, const AkvAttnDesc* tail) {
+    AttnPlan a, b;
+    if (!desc || !tail_matches(desc, tail) || plan_attention(desc, &a) || plan_attention(tail, &b)) return 0;
+    return a.ws + b.ws;
+}
+
+int akv_cuda_decode_attention_tail(const AkvAttnDesc* d, const AkvAttnDesc* tail, void* stream) {
+    if (!d || !tail_matches(d, tail)) return AKV_ERR_INVALID_ARGUMENT;
+    AttnPlan a, b;
+    if (int st = plan_attention(d, &a)) return st;
+    if (int st = plan_attention(tail, &b)) return st;
+    if (!d->q_dev || !d->out_dev) return AKV_ERR_INVALID_ARGUMENT;
+    if (!d->workspace_dev || d->workspace_bytes < a.ws + b.ws) return AKV_ERR_WORKSPACE;
+    if (reinterpret_cast<uintptr_t>(d->workspace_dev) % 16) return AKV_ERR_INVALID_ARGUMENT;
+    if (int st = ensure_init()) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int stride = a.nsplits + b.nsplits;
+    AttnParams pa = segment_params(d, a, d, 0, stride);
+    if (int st = launch_segment(d, a, pa, s, AKV_PHASE_SPLIT)) return st;
+    const AttnParams pb = segment_params(tail, b, d, a.nsplits, stride);
+    if (int st = launch_segment(tail, b, pb, s, AKV_PHASE_SPLIT)) return st;
+    // One merge over both segments' split rows (empty splits hold m = -inf).
+    pa.merge_all = 1;
+    merge_kernel<<<dim3(pa.Hq, pa.B), 128, 0, s>>>(pa, d->head_dim);
+    return launch_status();
 }
 
 int akv_cuda_decode_attention_noalloc(const AkvAttnDesc* d, void* stream) {

@@ -156,6 +156,22 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc);
  * pointer may be NULL. Returns the status akv_cuda_decode_attention would
  * return for a descriptor error. No counterpart in the reference (its Metal
  * host picks kernels in the probe programs). */
+/*
+ * Decode attention over two KV segments in one softmax: `desc` (for example
+ * the ASTC-compressed complete pages) and `tail` (for example the exact
+ * FP16 tokens of the incomplete last page that is not compressed yet).
+ * Both descriptors describe the same batch, query/KV heads and head_dim;
+ * each has its own planes, lengths (seq_lens_dev), pages and split size.
+ * Query, output, scale, status and workspace are taken from `desc` (the
+ * tail's are ignored); the workspace must hold
+ * akv_cuda_attention_tail_workspace(desc, tail) bytes. Output is
+ * softmax(scale q.[K;K_tail]^T) [V;V_tail] per sequence. No counterpart in
+ * the reference: its encoder rejects incomplete pages (codec.py:132-133) and
+ * its pilot keeps the suffix in FP16 outside the kernels.
+ */
+size_t akv_cuda_attention_tail_workspace(const AkvAttnDesc* desc, const AkvAttnDesc* tail);
+int akv_cuda_decode_attention_tail(const AkvAttnDesc* desc, const AkvAttnDesc* tail, void* stream);
+
 #define AKV_KERNEL_GENERIC 0
 #define AKV_KERNEL_FAST 1
 int akv_cuda_attention_plan(const AkvAttnDesc* desc, int* kernel, int* split_tokens, int* nsplits);

@@ -95,6 +95,25 @@ def test_attention_descriptor_validation():
     assert lib.akv_cuda_decode_attention_phase(ct.byref(d), 7, None) == 1
 
 
+def test_tail_descriptor_validation():
+    """The two-segment entry point validates before touching the GPU."""
+    from astc_kv_cuda import _lib as L
+    lib = L.lib()
+    d = L.AkvAttnDesc()
+    d.batch, d.q_heads, d.kv_heads, d.head_dim, d.max_tokens, d.page_tokens = 1, 9, 3, 64, 384, 96
+    d.k.storage = d.v.storage = L.AKV_STORAGE_FP16
+    d.k.data = d.v.data = 4096
+    t = L.AkvAttnDesc.from_buffer_copy(d)
+    t.max_tokens = t.page_tokens = 32
+    assert lib.akv_cuda_attention_tail_workspace(ct.byref(d), None) == 0
+    assert lib.akv_cuda_decode_attention_tail(ct.byref(d), None, None) == 1
+    ws = lib.akv_cuda_attention_tail_workspace(ct.byref(d), ct.byref(t))
+    assert ws == lib.akv_cuda_attention_workspace(ct.byref(d)) + lib.akv_cuda_attention_workspace(ct.byref(t))
+    t.kv_heads = 1  # a tail must describe the same heads
+    assert lib.akv_cuda_attention_tail_workspace(ct.byref(d), ct.byref(t)) == 0
+    assert lib.akv_cuda_decode_attention_tail(ct.byref(d), ct.byref(t), None) == 1
+
+
 def test_restore_plane_validation():
     from astc_kv_cuda import _lib as L
     p = L.AkvPlane()

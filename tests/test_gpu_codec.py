@@ -53,3 +53,24 @@ def test_codec_attention_mirror_positions(cuda):
     got16, _ = A.attention(q, k[0].astype(np.float16), ev, pos)
     ref16, _ = O.attention(q, k[0].astype(np.float16).astype(np.float32), ev.decoded, pos)
     assert_attention_close(got16, ref16, "fp16 K plane")
+
+
+def test_codec_attention_mirror_fresh_tail(cuda):
+    """codec.attention with an FP16 tail: positions past the encoded pages
+    attend the tail tokens in the same softmax."""
+    import astc_kv_cuda as A
+    rng = np.random.default_rng(13)
+    k, _ = kv_values(rng, 1, 3, 192, 64)
+    v, _ = kv_values(rng, 1, 3, 192, 64)
+    kt, _ = kv_values(rng, 1, 3, 40, 64)
+    vt, _ = kv_values(rng, 1, 3, 40, 64)
+    ek = A.encode_tensor(k[0], {"block": 6, "layout": "scalar", "normalization": "page_channel"}, quality=60)
+    ev = A.encode_tensor(v[0], {"block": 6, "layout": "scalar", "normalization": "token"}, quality=60)
+    q = rng.standard_normal((9, 4, 64)).astype(np.float32)
+    pos = np.array([231, 200, 191, 10])
+    kt16, vt16 = kt[0].astype(np.float16), vt[0].astype(np.float16)
+    got, _ = A.attention(q, ek, ev, pos, k_tail=kt16, v_tail=vt16)
+    kall = np.concatenate([ek.decoded, kt16.astype(np.float32)], axis=1)
+    vall = np.concatenate([ev.decoded, vt16.astype(np.float32)], axis=1)
+    ref, _ = O.attention(q, kall, vall, pos)
+    assert_attention_close(got, ref, "codec.attention mirror with FP16 tail")
