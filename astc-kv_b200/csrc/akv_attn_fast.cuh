@@ -187,7 +187,9 @@ __device__ __noinline__ void eval_block_generic(uint4 blk, int norm, float sc, f
 template <int NB, int NT, int BS>
 struct DecodeScratch {
     static constexpr int N = BS * BS;
-    static constexpr int kSlowCap = NB < 32 ? NB : 32;
+    // Descriptor slots: every block of a small chunk (8x8 planes are mostly
+    // reduced grids), at most 64.
+    static constexpr int kSlowCap = NB < 64 ? NB : 64;
     // Columns: one per decoding thread (a chunk with fewer blocks than
     // threads leaves the others idle).
     static constexpr int NC = NT < ((NB + 31) / 32) * 32 ? NT : ((NB + 31) / 32) * 32;
@@ -196,7 +198,7 @@ struct DecodeScratch {
     int nslot;                  // descriptor slots taken in this plane-chunk
     uint16_t slow_blk[kSlowCap];
     BlockDesc<1> desc[kSlowCap];
-    uint8_t w[kSlowCap][64];
+    uint8_t w[kSlowCap][72];    // grid weights (+ 8 bytes of slack for the infill taps)
 };
 
 // Texels of one table / constant block -> the hi/lo tiles (pairs of columns
@@ -328,9 +330,16 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
             const int br = i / cols, bc = i - br * cols;
             const int row = br * BS + y, col = bc * BS + x;
             if (col >= D) continue;
-            uint32_t cv[1];
-            texel_values<BS, 1>(ds.desc[slot], ds.w[slot], x, y, cv);
-            const float u = c16_to_unit(cv[0]);
+            const BlockDesc<1>& d = ds.desc[slot];
+            uint32_t c16;
+            if (d.info & ((1u << kInfoVoid) | (1u << kInfoError) | (1u << kInfoDual))) {
+                uint32_t cv[1];
+                texel_values<BS, 1>(d, ds.w[slot], x, y, cv);
+                c16 = cv[0];
+            } else {
+                c16 = desc_texel_c16<BS>(d, ds.w[slot], t);
+            }
+            const float u = c16_to_unit(c16);
             float s, o;
             if (affine) { s = __half2float(mscl[i]); o = __half2float(moff[i]); }
             else if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row]); o = __half2float(moff[row]); }

@@ -342,6 +342,30 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
     }
 }
 
+// UNORM16 value C of texel t of a single-plane descriptor (what texel_values
+// gives for it) through the host-built infill taps; w must have 8 readable
+// bytes of slack past the grid (taps past the grid carry weight 0).
+template <int BS>
+__device__ __forceinline__ uint32_t desc_texel_c16(const BlockDesc<1>& d, const uint8_t* w, int t) {
+    constexpr int fp = footprint_index(BS);
+    const uint32_t info = d.info;
+    uint32_t wt;
+    if (info & (1u << kInfoReduced)) {
+        const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
+        const uint32_t tap = __ldg(&g_akv_tables.infill[fp][wx - 2][wy - 2][t]);
+        const uint32_t i00 = tap & 63u, fs = (tap >> 6) & 15u, ft = tap >> 10;
+        const uint32_t w11 = (fs * ft + 8u) >> 4;
+        wt = (w[i00] * (16u - fs - ft + w11) + w[i00 + 1] * (fs - w11) + w[i00 + wx] * (ft - w11) +
+              w[i00 + wx + 1] * w11 + 8u) >> 4;
+    } else {
+        wt = w[t];
+    }
+    const uint32_t word = t < 16 ? d.pat[0] : t < 32 ? d.pat[1] : t < 48 ? d.pat_hi[0] : d.pat_hi[1];
+    const uint32_t ep = d.ep[(word >> (2 * (t & 15))) & 3u];
+    const uint32_t X = (ep & 0xFFu) * (64u - wt) + ((ep >> 8) & 0xFFu) * wt;
+    return 4u * X + ((X + 32u) >> 6);
+}
+
 // fp32 value of texel t of a table / constant block (host emulation and
 // checks; the kernel's tile writer reads the same table).
 __device__ __forceinline__ float lum_unit(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt, int t) {

@@ -252,6 +252,19 @@ void build_tables(Tables* t) {
         t->dig3[v] = d;
     }
     for (int v = 0; v < 128; ++v) t->dig3[256 + v] = t->quint[v];
+    for (int f = 0; f < kNumFootprints; ++f) {
+        const int bs = f == 0 ? 4 : (f == 1 ? 6 : 8);
+        const int ds = (1024 + bs / 2) / (bs - 1);
+        for (int wx = 2; wx <= bs; ++wx)
+            for (int wy = 2; wy <= bs; ++wy)
+                for (int y = 0; y < bs; ++y)
+                    for (int x = 0; x < bs; ++x) {
+                        const int gs = (ds * x * (wx - 1) + 32) >> 6, gt = (ds * y * (wy - 1) + 32) >> 6;
+                        const int i00 = (gs >> 4) + (gt >> 4) * wx;
+                        t->infill[f][wx - 2][wy - 2][y * bs + x] =
+                            static_cast<uint16_t>(i00 | ((gs & 15) << 6) | ((gt & 15) << 10));
+                    }
+    }
     static const int kBlocks[kNumFootprints] = {4, 6, 8};
     for (int f = 0; f < kNumFootprints; ++f) {
         const int bs = kBlocks[f];

@@ -48,6 +48,11 @@ struct Tables {
     // Digits of a trit block (index 0..255) or quint block (256 + 0..127),
     // 3 bits per digit: the runtime BISE decoder's single lookup.
     uint16_t dig3[384];
+    // Bilinear infill taps of a reduced weight grid (spec weight infill) for
+    // footprint f, grid (wx, wy) in 2..8 x 2..8, texel t: base grid index
+    // i00 | fs << 6 | ft << 10. At the last texel row / column the fraction
+    // is 0, so the taps past the grid get zero weight.
+    uint16_t infill[kNumFootprints][7][7][64];
 };
 
 // Fills `t` on the host. Deterministic; no device calls.

@@ -69,8 +69,8 @@ extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 // + weight codes, or per-texel endpoint/weight evaluation for 4x4, read back as
 // the kernel's tile writer reads them) or
 // descriptor blocks (evaluated per texel as the kernel's phase 1b does).
-// Returns the fp16-view values of the R channel per texel, or -1 for blocks
-// that take the generic path; `cls` gets the kind.
+// Generic blocks are evaluated as the kernel's phase 1b does. Returns the
+// fp16-view values of the R channel per texel; `cls` gets the kind.
 template <int BS>
 static int fast_r_one(uint4 b, int* kind_out, float* out) {
     namespace F = akv::fast;
@@ -79,20 +79,38 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
     int cq;
     const int kind = F::block_kind<BS>(b, me, cq);
     *kind_out = kind;
-    if (kind == F::kKindGeneric) { for (int t = 0; t < N; ++t) out[t] = -1.f; return 0; }
+    if (kind == F::kKindGeneric) {
+        // The kernel's generic slots: decode_header, then phase 1b's choice of
+        // evaluator (lean infill taps unless void / error / dual plane).
+        akv::BlockDesc<1> d;
+        uint8_t w[72];
+        std::memset(w, 0xEE, sizeof(w));
+        akv::decode_header<1>(b, akv::footprint_index(BS), d, w);
+        const bool lean = !(d.info & ((1u << akv::kInfoVoid) | (1u << akv::kInfoError) | (1u << akv::kInfoDual)));
+        for (int t = 0; t < N; ++t) {
+            uint32_t c;
+            if (lean) {
+                c = F::desc_texel_c16<BS>(d, w, t);
+            } else {
+                uint32_t cv[1];
+                akv::texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
+                c = cv[0];
+            }
+            out[t] = akv::c16_to_unit(c);
+        }
+        return 0;
+    }
     uint32_t tab[F::kTabCapMax];
     uint8_t codes[64 + akv::fast::kCodePad];
     std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
     akv::BlockDesc<1> d;
-    uint8_t w[64];
-    std::memset(w, 0, sizeof(w));
+    uint8_t w[72];
+    std::memset(w, 0xEE, sizeof(w));  // stale slack bytes must not matter
     F::LumOut o;
     F::decode_lum<BS>(b, kind, me, cq, false, 0.f, 0.f, tab, codes, 1, kind == F::kKindDesc ? &d : nullptr, w, o);
     for (int t = 0; t < N; ++t) {
         if (kind == F::kKindDesc) {
-            uint32_t cv[1];
-            akv::texel_values<BS, 1>(d, w, t % BS, t / BS, cv);
-            out[t] = akv::c16_to_unit(cv[0]);
+            out[t] = akv::c16_to_unit(F::desc_texel_c16<BS>(d, w, t));
         } else if constexpr (F::kDirect<BS>) {
             out[t] = F::direct_unit(o, codes, 1, t);
         } else {
