@@ -52,64 +52,6 @@ __device__ __forceinline__ uint32_t table_entry(float u, bool affine, float sc, 
     return static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
 }
 
-// The first nv (<= 8) colour integers of range `cq` from a colour stream
-// that starts at bit 0 of (clo, chi) and is masked to its length, unquantised
-// to 0..255 into registers (no local-memory arrays); v[nv..7] = 0.
-__device__ __forceinline__ void colors8(uint64_t clo, uint64_t chi, int cq, int nv, int (&v)[8]) {
-    const Tables& T = g_akv_tables;
-    const uint32_t shp = __ldg(&T.shape[cq]);
-    const int b = shp & 15;
-    const uint64_t mm = (1ull << b) - 1ull;
-    const uint8_t* un = T.cunq[cq];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0;
-    if (shp & 0x10) {
-        const int gb = 5 * b + 8;
-#pragma unroll
-        for (int g = 0; g < 2; ++g) {
-            if (5 * g >= nv) break;
-            const uint64_t w = window_u128(clo, chi, g * gb);
-            const uint32_t t = static_cast<uint32_t>((w >> b) & 3u) | static_cast<uint32_t>(((w >> (2 * b + 2)) & 3u) << 2) |
-                               static_cast<uint32_t>(((w >> (3 * b + 4)) & 1u) << 4) |
-                               static_cast<uint32_t>(((w >> (4 * b + 5)) & 3u) << 5) |
-                               static_cast<uint32_t>(((w >> (5 * b + 7)) & 1u) << 7);
-            const uint32_t dg = __ldg(&T.trit[t]);
-            const int off[5] = {0, 2, 4, 5, 7};
-#pragma unroll
-            for (int j = 0; j < 5; ++j) {
-                const int i = 5 * g + j;
-                if (i < 8 && i < nv) {
-                    const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
-                    v[i] = __ldg(un + ((((dg >> (2 * j)) & 3u) << b) | m));
-                }
-            }
-        }
-    } else if (shp & 0x20) {
-        const int gb = 3 * b + 7;
-#pragma unroll
-        for (int g = 0; g < 3; ++g) {
-            if (3 * g >= nv) break;
-            const uint64_t w = window_u128(clo, chi, g * gb);
-            const uint32_t qv = static_cast<uint32_t>((w >> b) & 7u) | static_cast<uint32_t>(((w >> (2 * b + 3)) & 3u) << 3) |
-                                static_cast<uint32_t>(((w >> (3 * b + 5)) & 3u) << 5);
-            const uint32_t dg = __ldg(&T.quint[qv]);
-            const int off[3] = {0, 3, 5};
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const int i = 3 * g + j;
-                if (i < 8 && i < nv) {
-                    const uint32_t m = static_cast<uint32_t>((w >> (j * b + off[j])) & mm);
-                    v[i] = __ldg(un + ((((dg >> (3 * j)) & 7u) << b) | m));
-                }
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (i < nv) v[i] = __ldg(un + static_cast<uint32_t>(window_u128(clo, chi, i * b) & mm));
-    }
-}
-
 // UNORM16 value of a constant block: the void-extent R colour, or the error
 // colour's R = 1.0 for illegal encodings.
 __device__ __forceinline__ uint32_t const_c16(uint4 blk) {
@@ -203,6 +145,49 @@ __device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, i
         w1 = __funnelshift_r(w1, w2, gb);
         w2 = __funnelshift_r(w2, w3, gb);
         w3 >>= gb;
+    }
+}
+
+// The first nv (<= 8) colour integers of range cq from the colour stream
+// (s0, s1), masked to its length, unquantised to 0..255 into out[j * nt]:
+// one runtime step loop for trit, quint and plain-bit ranges alike (64-bit
+// windows: colour groups reach 40 bits). Writes up to four values past nv
+// (callers have the slack).
+__device__ __forceinline__ void color_values(uint64_t s0, uint64_t s1, int cq, int nv, uint8_t* out, int nt) {
+    const Tables& T = g_akv_tables;
+    const uint32_t shp = __ldg(&T.shape[cq]);
+    const int b = shp & 15;
+    const bool tr = (shp >> 4) & 1, qu = (shp >> 5) & 1;
+    const int gs = qu ? 3 : 5;
+    const int gb = tr ? 5 * b + 8 : (qu ? 3 * b + 7 : 5 * b);
+    const int ng = qu ? (nv + 2) / 3 : (nv + 4) / 5;
+    const uint64_t m1 = tr ? 0x03u : (qu ? 0x07u : 0u);
+    const uint64_t m2 = tr ? 0x0Cu : (qu ? 0x18u : 0u);
+    const uint64_t m3 = tr ? 0x10u : (qu ? 0x60u : 0u);
+    const uint64_t m4 = tr ? 0x60u : 0u;
+    const uint64_t m5 = tr ? 0x80u : 0u;
+    const int o1 = b + (tr ? 2 : (qu ? 3 : 0));
+    const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
+    const int o3 = 3 * b + (tr ? 5 : 0);
+    const int o4 = 4 * b + (tr ? 7 : 0);
+    const uint16_t* dig = T.dig3 + (qu ? 256 : 0);
+    const uint8_t* un = T.cunq[cq];
+    const uint64_t bm = (1ull << b) - 1ull;
+    uint8_t* cp = out;
+    for (int g = 0; g < ng; ++g) {
+        const uint64_t win = s0;
+        const uint32_t X = static_cast<uint32_t>(((win >> b) & m1) | ((win >> (2 * b)) & m2) |
+                                                 ((win >> (3 * b)) & m3) | ((win >> (4 * b)) & m4) |
+                                                 ((win >> (5 * b)) & m5));
+        const uint32_t dg = __ldg(dig + X);
+        cp[0] = __ldg(un + (((dg & 7u) << b) | static_cast<uint32_t>(win & bm)));
+        cp[nt] = __ldg(un + ((((dg >> 3) & 7u) << b) | static_cast<uint32_t>((win >> o1) & bm)));
+        cp[2 * nt] = __ldg(un + ((((dg >> 6) & 7u) << b) | static_cast<uint32_t>((win >> o2) & bm)));
+        cp[3 * nt] = __ldg(un + ((((dg >> 9) & 7u) << b) | static_cast<uint32_t>((win >> o3) & bm)));
+        cp[4 * nt] = __ldg(un + ((((dg >> 12) & 7u) << b) | static_cast<uint32_t>((win >> o4) & bm)));
+        cp += gs * nt;
+        s0 = (s0 >> gb) | (s1 << (64 - gb));
+        s1 >>= gb;
     }
 }
 
@@ -304,11 +289,15 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
     }
     int v[8];
     {
+        // Colour integers through the thread's code rows (overwritten by the
+        // weight codes below), read back into registers.
         const int cstart = parts == 1 ? 17 : 29;
         uint64_t clo = window_u128(lo, hi, cstart);
         uint64_t chi = hi >> cstart;
         mask_u128(clo, chi, bise_stream_bits_dev(2 * parts, cq));
-        colors8(clo, chi, cq, 2 * parts, v);
+        color_values(clo, chi, cq, 2 * parts, codes, nt);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = codes[k * nt];
     }
     if constexpr (kDirect<BS>) {
         o.e0p = static_cast<uint32_t>(v[0] | (v[2] << 8) | (v[4] << 16) | (v[6] << 24));
