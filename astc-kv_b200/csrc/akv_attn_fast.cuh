@@ -2,7 +2,8 @@
 // ASTC K) on sm_100a.
 //
 // Per CTA: one (split, kv head, batch) unit, processed in chunks of CH tokens
-// (CH = 48 for 6x6 footprints, 64 otherwise; a chunk never crosses a page).
+// (CH = 48 with a 6x6 plane, 32 when K is ASTC too, 64 otherwise; a chunk
+// never crosses a page), 64 threads per 16-token tile.
 //
 //   * Staging: one elected thread issues cp.async.bulk copies of the chunk's
 //     V blocks and fp16 metadata (and ASTC K blocks) into a two-stage shared
@@ -91,17 +92,10 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
-// 16-byte global -> shared asynchronous copy (LDGSTS), completed by
-// cp.async.wait_group.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// L2 prefetch of one global-memory line.
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
-
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {

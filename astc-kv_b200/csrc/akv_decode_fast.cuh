@@ -355,8 +355,8 @@ __device__ __forceinline__ uint32_t desc_texel_c16(const BlockDesc<1>& d, const 
     return 4u * X + ((X + 32u) >> 6);
 }
 
-// fp32 value of texel t of a table / constant block (host emulation and
-// checks; the kernel's tile writer reads the same table).
+// fp32 value of texel t of a table / constant block (for host-side checks;
+// the kernel's tile writer reads the table the same way).
 __device__ __forceinline__ float lum_unit(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt, int t) {
     const uint32_t c = codes[t * nt] & o.cmask;
     const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
