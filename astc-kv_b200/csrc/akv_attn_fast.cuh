@@ -131,10 +131,11 @@ __device__ __forceinline__ void split_pair(float v0, float v1, uint32_t& hi, uin
     lo = pack_h2(v0 - hf.x, v1 - hf.y);
 }
 
-// Bytes of metadata per chunk for a plane.
+// Metadata elements per chunk for a plane (a chunk of CH tokens spans
+// max(1, CH / P) pages of P tokens; page-channel metadata is per page).
 template <int BS>
-__device__ __forceinline__ int meta_elems(int norm, int cols, int CH, int D) {
-    return norm == AKV_NORM_BLOCK_AFFINE ? (CH / BS) * cols : (norm == AKV_NORM_TOKEN ? CH : D);
+__device__ __forceinline__ int meta_elems(int norm, int cols, int CH, int D, int P) {
+    return norm == AKV_NORM_BLOCK_AFFINE ? (CH / BS) * cols : (norm == AKV_NORM_TOKEN ? CH : D * (P < CH ? CH / P : 1));
 }
 
 template <int BS>
@@ -344,9 +345,99 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
     }
 }
 
+// One RGBA texel (four channel values v[0..3] of channels col..col+3) -> the
+// hi/lo tiles, two 8-byte stores.
+template <int LD>
+__device__ __forceinline__ void put_rgba(const float (&v)[4], bool ok, int row, int col, __half (*thi)[LD],
+                                         __half (*tlo)[LD]) {
+    uint32_t h0, l0, h1, l1;
+    split_pair(v[0], v[1], h0, l0);
+    split_pair(v[2], v[3], h1, l1);
+    if (!ok) h0 = l0 = h1 = l1 = 0u;
+    *reinterpret_cast<uint2*>(&thi[row][col]) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(&tlo[row][col]) = make_uint2(l0, l1);
+}
+
+// Affine of channel `ch` in token row `row` of block i (meta indexing as in
+// decode_plane).
+__device__ __forceinline__ void meta_affine(int norm, const __half* moff, const __half* mscl, int i, int row, int ch,
+                                            float& s, float& o) {
+    const int m = norm == AKV_NORM_BLOCK_AFFINE ? i : (norm == AKV_NORM_TOKEN ? row : ch);
+    s = __half2float(mscl[m]);
+    o = __half2float(moff[m]);
+}
+
+// Whole RGBA 4x4 block decoded and evaluated by one thread with the generic
+// decoder (out of line: blocks the fast path does not cover).
+template <int LD>
+__device__ __noinline__ void eval_rgba_generic(uint4 blk, int i, int norm, const __half* moff, const __half* mscl,
+                                               int row0, int col0, int rows, __half (*thi)[LD], __half (*tlo)[LD]) {
+    BlockDesc<4> d;
+    uint8_t w[64];
+    decode_header<4>(blk, footprint_index(4), d, w);
+    for (int t = 0; t < 16; ++t) {
+        const int x = t & 3, y = t >> 2;
+        uint32_t c[4];
+        texel_values<4, 4>(d, w, x, y, c);
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float s, o;
+            meta_affine(norm, moff, mscl, i, row0 + y, col0 + 4 * x + k, s, o);
+            v[k] = fmaf(c16_to_unit(c[k]), s, o);
+        }
+        put_rgba<LD>(v, y < rows, row0 + y, col0 + 4 * x, thi, tlo);
+    }
+}
+
+// Decode one RGBA 4x4 plane's chunk into the hi/lo tiles (block i covers
+// token rows 4 br.. and channels 16 bc..). All threads call it.
+template <int D, int THREADS, int NB, int LD>
+__device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half* moff, const __half* mscl, int norm,
+                                                  int cols, int rows_blk, int n, bool valid, int P,
+                                                  DecodeScratch<NB, THREADS, 4>& ds, __half (*thi)[LD],
+                                                  __half (*tlo)[LD]) {
+    constexpr int NC = DecodeScratch<NB, THREADS, 4>::NC;
+    const int nblk = rows_blk * cols;
+    const int tid = threadIdx.x;
+    for (int i = tid; i < nblk; i += THREADS) {
+        const uint4 blk = raw[i];
+        const int br = i / cols, bc = i - br * cols;
+        const int row0 = br * 4, col0 = bc * 16;
+        const int rows = valid ? min(4, n - row0) : 0;
+        // Page-channel metadata of the page this block row lies in.
+        const int pm = norm == AKV_NORM_PAGE_CHANNEL ? (row0 / P) * D : 0;
+        const __half* bmoff = moff + pm;
+        const __half* bmscl = mscl + pm;
+        uint32_t me;
+        int cq;
+        const int kind = rgba_block_kind(blk, me, cq);
+        if (kind == kKindGeneric) {
+            eval_rgba_generic<LD>(blk, i, norm, bmoff, bmscl, row0, col0, rows, thi, tlo);
+            continue;
+        }
+        RgbaOut o;
+        uint8_t* codes = &ds.codes[0][tid];
+        decode_rgba4(blk, kind, me, cq, codes, NC, o);
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+            const int x = t & 3, y = t >> 2;
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float s, of;
+                meta_affine(norm, bmoff, bmscl, i, row0 + y, col0 + 4 * x + k, s, of);
+                v[k] = fmaf(c16_to_unit(rgba_c16(o, codes, NC, t, k)), s, of);
+            }
+            put_rgba<LD>(v, y < rows, row0 + y, col0 + 4 * x, thi, tlo);
+        }
+    }
+    __syncthreads();
+}
+
 // ------------------------------------------------------------------ kernel
 
-template <int D, int G, int VBS, int KBS>
+template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
 struct Cfg {
     // Tokens per chunk: 48 with a 6x6 plane; 32 with ASTC K (two decoded
     // planes in shared memory); else 64.
@@ -354,13 +445,17 @@ struct Cfg {
     static constexpr int NWM = CH / 16;                        // token tiles of 16 per chunk
     static constexpr int THREADS = 64 * NWM;                   // two warps per token tile
     static constexpr int LD = D + 8;                           // halves per tile row (16-byte pad)
-    static constexpr int VCOLS = (D + VBS - 1) / VBS;
+    // V block columns: a scalar block covers VBS channels, an RGBA block 4 x VBS.
+    static constexpr int VCOLS = VL == AKV_LAYOUT_RGBA ? D / (4 * VBS) : (D + VBS - 1) / VBS;
     static constexpr int VROWS = CH / VBS;
     static constexpr int VBLK = VROWS * VCOLS;
     static constexpr int KCOLS = KBS ? (D + KBS - 1) / KBS : 1;
     static constexpr int KROWS = KBS ? CH / KBS : 0;
     static constexpr int KBLK = KROWS * KCOLS;
-    static constexpr int META = (VBLK > CH ? (VBLK > D ? VBLK : D) : (CH > D ? CH : D));
+    // V metadata per chunk; RGBA planes may have pages of 16 tokens inside a
+    // chunk (page-channel metadata of up to CH / 16 pages).
+    static constexpr int META0 = (VBLK > CH ? (VBLK > D ? VBLK : D) : (CH > D ? CH : D));
+    static constexpr int META = VL == AKV_LAYOUT_RGBA && D * (CH / 16) > META0 ? D * (CH / 16) : META0;
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
@@ -369,11 +464,12 @@ struct Cfg {
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
+    static_assert(VL == AKV_LAYOUT_SCALAR || (VBS == 4 && KBS == 0 && D % 16 == 0), "RGBA: 4x4 V, FP16 K");
 };
 
-template <int D, int G, int VBS, int KBS>
+template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
 struct Smem {
-    using C = Cfg<D, G, VBS, KBS>;
+    using C = Cfg<D, G, VBS, KBS, VL>;
     uint64_t bar[2];
     int valid[2];
     __align__(16) uint4 vraw[2][C::VBLK];
@@ -393,10 +489,10 @@ struct Smem {
     float wl[C::NWM][8];
 };
 
-template <int D, int G, int VBS, int KBS>
-__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_kernel(AttnParams p) {
-    using C = Cfg<D, G, VBS, KBS>;
-    using S = Smem<D, G, VBS, KBS>;
+template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
+__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, 3) attn_fast_kernel(AttnParams p) {
+    using C = Cfg<D, G, VBS, KBS, VL>;
+    using S = Smem<D, G, VBS, KBS, VL>;
     constexpr int CH = C::CH, NWM = C::NWM, THREADS = C::THREADS, LD = C::LD;
     static_assert(THREADS == 64 * NWM, "every warp owns one (token tile, dim half)");
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -439,13 +535,13 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         const __half* voff = nullptr;
         const __half* vscl = nullptr;
         const int vrows = CH / VBS, vcols = C::VCOLS;
-        const int vme = meta_elems<VBS>(p.v.norm, vcols, CH, D);
+        const int vme = meta_elems<VBS>(p.v.norm, vcols, CH, D, P);
         const uint8_t* ksrc = nullptr;
         const __half* koff = nullptr;
         const __half* kscl = nullptr;
         const uint8_t* kside = nullptr;
         const int krows = KBS ? CH / KBS : 0, kcols = C::KCOLS;
-        const int kme = KBS ? meta_elems<(KBS ? KBS : 4)>(p.k.norm, kcols, CH, D) : 0;
+        const int kme = KBS ? meta_elems<(KBS ? KBS : 4)>(p.k.norm, kcols, CH, D, P) : 0;
         if (phys >= 0) {
             vsrc = p.v.data + b * p.v.sB + h * p.v.sH + static_cast<int64_t>(phys) * p.v.sP +
                    static_cast<int64_t>(tin / VBS) * vcols * 16;
@@ -548,10 +644,16 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS>::THREADS, 3) attn_fast_ker
         const bool valid = sm.valid[s] != 0;
         prefetch_k(c + 1);
         // Decode V (and K) tiles.
-        decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
-                                                  CH / VBS, n, valid,
-                                                  *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds), sm.vhi,
-                                                  sm.vlo);
+        if constexpr (VL == AKV_LAYOUT_RGBA)
+            decode_plane_rgba<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
+                                                      CH / 4, n, valid, P,
+                                                      *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, 4>*>(sm.ds),
+                                                      sm.vhi, sm.vlo);
+        else
+            decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
+                                                      C::VCOLS, CH / VBS, n, valid,
+                                                      *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds),
+                                                      sm.vhi, sm.vlo);
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;

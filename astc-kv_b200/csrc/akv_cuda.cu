@@ -126,11 +126,11 @@ int launch_attention(const AttnParams& p, cudaStream_t s, int phases) {
 
 using Launcher = int (*)(const AttnParams&, cudaStream_t, int);
 
-template <int D, int G, int VBS, int KBS>
+template <int D, int G, int VBS, int KBS, int VL>
 int launch_fast(const AttnParams& p, cudaStream_t s, int phases) {
-    using C = fast::Cfg<D, G, VBS, KBS>;
-    auto kern = fast::attn_fast_kernel<D, G, VBS, KBS>;
-    const size_t smem = sizeof(fast::Smem<D, G, VBS, KBS>);
+    using C = fast::Cfg<D, G, VBS, KBS, VL>;
+    auto kern = fast::attn_fast_kernel<D, G, VBS, KBS, VL>;
+    const size_t smem = sizeof(fast::Smem<D, G, VBS, KBS, VL>);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
         cudaGetLastError();
         return AKV_ERR_CUDA;
@@ -148,26 +148,29 @@ int launch_fast(const AttnParams& p, cudaStream_t s, int phases) {
 }
 
 struct FastVariant {
-    int D, G, vbs, kbs;
+    int D, G, vbs, kbs, vl;
     Launcher fn;
     size_t smem;
 };
 
 // Tensor-core variants for scalar-layout ASTC V with FP16 (kbs 0) or scalar
-// ASTC K.
-#define AKV_FAST(D, G, VB, KB) {D, G, VB, KB, &launch_fast<D, G, VB, KB>, sizeof(fast::Smem<D, G, VB, KB>)}
+// ASTC K, and RGBA-layout 4x4 V with FP16 K.
+#define AKV_FAST(D, G, VB, KB, VL) \
+    {D, G, VB, KB, VL, &launch_fast<D, G, VB, KB, VL>, sizeof(fast::Smem<D, G, VB, KB, VL>)}
+constexpr int kS = AKV_LAYOUT_SCALAR, kR = AKV_LAYOUT_RGBA;
 const FastVariant kFastVariants[] = {
-    AKV_FAST(64, 3, 6, 0), AKV_FAST(64, 3, 6, 6), AKV_FAST(64, 3, 4, 0), AKV_FAST(64, 3, 8, 0),
-    AKV_FAST(128, 4, 6, 0), AKV_FAST(128, 4, 4, 0), AKV_FAST(128, 4, 8, 0),
-    AKV_FAST(128, 8, 8, 4), AKV_FAST(128, 8, 8, 0), AKV_FAST(128, 8, 4, 0),
+    AKV_FAST(64, 3, 6, 0, kS), AKV_FAST(64, 3, 6, 6, kS), AKV_FAST(64, 3, 4, 0, kS), AKV_FAST(64, 3, 8, 0, kS),
+    AKV_FAST(128, 4, 6, 0, kS), AKV_FAST(128, 4, 4, 0, kS), AKV_FAST(128, 4, 8, 0, kS),
+    AKV_FAST(128, 8, 8, 4, kS), AKV_FAST(128, 8, 8, 0, kS), AKV_FAST(128, 8, 4, 0, kS),
+    AKV_FAST(64, 3, 4, 0, kR), AKV_FAST(128, 4, 4, 0, kR),
 };
 #undef AKV_FAST
 
 int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : (kbs ? 32 : 64); }
 
-const FastVariant* find_fast(int D, int G, int vbs, int kbs) {
+const FastVariant* find_fast(int D, int G, int vbs, int kbs, int vl) {
     for (const FastVariant& v : kFastVariants)
-        if (v.D == D && v.G == G && v.vbs == vbs && v.kbs == kbs) return &v;
+        if (v.D == D && v.G == G && v.vbs == vbs && v.kbs == kbs && v.vl == vl) return &v;
     return nullptr;
 }
 
@@ -175,12 +178,12 @@ bool aligned16(int64_t bytes) { return bytes % 16 == 0; }
 
 // Metadata elements per chunk for a plane, and their offset granularity
 // inside a page (both must keep the bulk copies 16-byte aligned).
-bool meta_copy_ok(const AkvPlane& pl, int D, int CH) {
-    const int cols = (D + pl.block - 1) / pl.block;
+bool meta_copy_ok(const AkvPlane& pl, int D, int CH, int P) {
+    const int cols = pl.layout == AKV_LAYOUT_RGBA ? D / (4 * pl.block) : (D + pl.block - 1) / pl.block;
     int64_t elems, step;
     if (pl.normalization == AKV_NORM_BLOCK_AFFINE) { elems = (CH / pl.block) * cols; step = elems; }
     else if (pl.normalization == AKV_NORM_TOKEN) { elems = CH; step = CH; }
-    else { elems = D; step = 0; }
+    else { elems = static_cast<int64_t>(D) * (P < CH ? CH / P : 1); step = 0; }
     return aligned16(elems * 2) && aligned16(step * 2) && aligned16(pl.meta_stride_batch * 2) &&
            aligned16(pl.meta_stride_head * 2) && aligned16(pl.meta_stride_page * 2) &&
            reinterpret_cast<uintptr_t>(pl.offsets) % 16 == 0 && reinterpret_cast<uintptr_t>(pl.scales) % 16 == 0;
@@ -189,9 +192,9 @@ bool meta_copy_ok(const AkvPlane& pl, int D, int CH) {
 bool fast_path_ok(const AkvAttnDesc* d, int kbs, int vbs, int vl, int split) {
     const char* env = std::getenv("AKV_ATTN_PATH");
     if (env && std::strcmp(env, "generic") == 0) return false;
-    if (!vbs || vl != AKV_LAYOUT_SCALAR) return false;
+    if (!vbs) return false;
     if (d->k.storage == AKV_STORAGE_ASTC && d->k.layout != AKV_LAYOUT_SCALAR) return false;
-    const FastVariant* fv = find_fast(d->head_dim, d->q_heads / d->kv_heads, vbs, kbs);
+    const FastVariant* fv = find_fast(d->head_dim, d->q_heads / d->kv_heads, vbs, kbs, vl);
     if (!fv) return false;
     int dev = 0, smem_max = 0;
     cudaGetDevice(&dev);
@@ -201,11 +204,23 @@ bool fast_path_ok(const AkvAttnDesc* d, int kbs, int vbs, int vl, int split) {
         return false;
     }
     const int CH = fast_chunk(kbs, vbs);
-    if (d->page_tokens % CH || split % CH) return false;
+    const int P = d->page_tokens;
+    if (split % CH) return false;
+    if (P % CH) {
+        // Several pages per chunk: RGBA V of a contiguous cache only, pages of
+        // at least 16 tokens, consecutive pages adjacent in memory (one copy
+        // per chunk) with their metadata.
+        if (vl != AKV_LAYOUT_RGBA || d->block_table_dev || CH % P || P < 16) return false;
+        const AkvPlane& v = d->v;
+        const int cols = d->head_dim / (4 * v.block);
+        const int64_t per_page = v.normalization == AKV_NORM_BLOCK_AFFINE ? (P / v.block) * cols
+                                 : v.normalization == AKV_NORM_TOKEN ? P : d->head_dim;
+        if (v.stride_page != static_cast<int64_t>(P / v.block) * cols * 16 || v.meta_stride_page != per_page) return false;
+    }
     const AkvPlane* planes[2] = {&d->k, &d->v};
     for (const AkvPlane* pl : planes) {
         if (!aligned16(pl->stride_batch) || !aligned16(pl->stride_head) || !aligned16(pl->stride_page)) return false;
-        if (pl->storage == AKV_STORAGE_ASTC && !meta_copy_ok(*pl, d->head_dim, CH)) return false;
+        if (pl->storage == AKV_STORAGE_ASTC && !meta_copy_ok(*pl, d->head_dim, CH, P)) return false;
     }
     if (d->k.side) {
         if (d->k.side_count > 8) return false;
@@ -295,8 +310,7 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
     out->vbs = fps[1];
     out->vl = d->v.storage == AKV_STORAGE_ASTC ? d->v.layout : AKV_LAYOUT_SCALAR;
     if (!find_variant(d->head_dim, d->q_heads / d->kv_heads, out->kbs, out->vbs, out->vl)) return AKV_ERR_UNSUPPORTED;
-    const bool fast_shape = out->vbs && out->vl == AKV_LAYOUT_SCALAR &&
-                            find_fast(d->head_dim, d->q_heads / d->kv_heads, out->vbs, out->kbs);
+    const bool fast_shape = out->vbs && find_fast(d->head_dim, d->q_heads / d->kv_heads, out->vbs, out->kbs, out->vl);
     const int ch = fast_shape ? fast_chunk(out->kbs, out->vbs) : chunk_tokens(out->kbs, out->vbs);
     int split = d->split_tokens;
     if (split <= 0) {
@@ -376,7 +390,7 @@ AttnParams segment_params(const AkvAttnDesc* d, const AttnPlan& plan, const AkvA
 }
 
 int launch_segment(const AkvAttnDesc* d, const AttnPlan& plan, const AttnParams& p, cudaStream_t s, int phase) {
-    if (plan.fast) return find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs)->fn(p, s, phase);
+    if (plan.fast) return find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs, plan.vl)->fn(p, s, phase);
     return find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl)->fn(p, s, phase);
 }
 

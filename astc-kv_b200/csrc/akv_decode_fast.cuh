@@ -363,5 +363,114 @@ __device__ __forceinline__ float lum_unit(const LumOut& o, const uint32_t* tab, 
     return __uint_as_float(tab[(part * o.L + c) * nt]);
 }
 
+// ------------------------------------------------- RGBA layout, 4x4 blocks
+//
+// A texel holds four consecutive channels (codec.py:185-187). Fast blocks:
+// one weight plane, full 4x4 grid, at most two partitions, RGBA-direct
+// endpoints (mode 12) on every partition; each texel's four values are
+// computed from its endpoints and weight in the decoding thread.
+
+// Kind of an RGBA 4x4 block (kKindTable = the fast path), with its mode
+// entry and colour range.
+__device__ __forceinline__ int rgba_block_kind(uint4 blk, uint32_t& me, int& cq) {
+    constexpr int fp = footprint_index(4);
+    const uint32_t x = blk.x;
+    const int mode = static_cast<int>(x & 0x7FF);
+    me = 0u;
+    cq = 0;
+    if ((mode & 0x1FF) == 0x1FC) return kKindConst;
+    me = __ldg(&g_akv_tables.mode[fp][mode]);
+    if (!(me & kModeValid)) return kKindConst;
+    if (me & (kModeDual | kModeReduced)) return kKindGeneric;
+    const int parts = static_cast<int>((x >> 11) & 3) + 1;
+    if (parts > 2) return kKindGeneric;
+    const bool rgba = parts == 1 ? ((x >> 13) & 15) == 12 : ((x >> 23) & 0x3F) == (12 << 2);
+    if (!rgba) return kKindGeneric;
+    const int avail = 128 - mode_wbits(me) - (parts == 1 ? 17 : 29);
+    cq = avail < 0 ? 0xFF : __ldg(&g_akv_tables.cquant[4 * parts][avail]);
+    return cq == 0xFF ? kKindConst : kKindTable;
+}
+
+// What the tile writer needs of a fast or constant RGBA block.
+struct RgbaOut {
+    uint32_t e0[4], e1[4];  // per channel: endpoints of partitions 0, 1 as bytes 0, 1
+    uint32_t pat;           // partition per texel, 2 bits each
+    const uint8_t* wun;     // weight unquantisation row
+    bool cst;               // constant block: c16 holds the four channel values
+    uint32_t c16[4];
+};
+
+// Fast or constant RGBA 4x4 block -> RgbaOut and the 16 weight codes in
+// codes[t * nt] (which also stage the colour integers).
+__device__ __forceinline__ void decode_rgba4(uint4 blk, int kind, uint32_t me, int cq, uint8_t* codes, int nt,
+                                             RgbaOut& o) {
+    const Tables& T = g_akv_tables;
+    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
+    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
+    o.cst = kind == kKindConst;
+    o.pat = 0u;
+    o.wun = T.wunq[mode_wq(me)];
+    if (o.cst) {
+        const uint32_t err[4] = {0xFFFFu, 0u, 0xFFFFu, 0xFFFFu};  // error colour (1, 0, 1, 1)
+        // A valid void extent carries RGBA UNORM16 in bits 64..127.
+        bool valid_void = false;
+        if ((blk.x & 0x1FF) == 0x1FC) {
+            const uint32_t s0 = static_cast<uint32_t>(lo >> 12) & 0x1FFF, s1 = static_cast<uint32_t>(lo >> 25) & 0x1FFF;
+            const uint32_t t0 = static_cast<uint32_t>(lo >> 38) & 0x1FFF, t1 = static_cast<uint32_t>(lo >> 51) & 0x1FFF;
+            const bool all_ones = (s0 & s1 & t0 & t1) == 0x1FFF;
+            valid_void = !(blk.x & 0x200) && ((blk.x >> 10) & 3) == 3 && (all_ones || (s0 < s1 && t0 < t1));
+        }
+        o.c16[0] = valid_void ? (blk.z & 0xFFFFu) : err[0];
+        o.c16[1] = valid_void ? (blk.z >> 16) : err[1];
+        o.c16[2] = valid_void ? (blk.w & 0xFFFFu) : err[2];
+        o.c16[3] = valid_void ? (blk.w >> 16) : err[3];
+        return;
+    }
+    const int parts = static_cast<int>((lo >> 11) & 3) + 1;
+    {
+        const int cstart = parts == 1 ? 17 : 29;
+        uint64_t clo = window_u128(lo, hi, cstart);
+        uint64_t chi = hi >> cstart;
+        mask_u128(clo, chi, bise_stream_bits_dev(8 * parts, cq));
+        color_values(clo, chi, cq, 8 * parts, codes, nt);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o.e0[c] = o.e1[c] = 0u;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        if (q < parts) {
+            int v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = codes[(8 * q + k) * nt];
+            int a[4], b[4];
+            if (v[1] + v[3] + v[5] >= v[0] + v[2] + v[4]) {
+                a[0] = v[0]; a[1] = v[2]; a[2] = v[4]; a[3] = v[6];
+                b[0] = v[1]; b[1] = v[3]; b[2] = v[5]; b[3] = v[7];
+            } else {  // blue contraction, endpoints swapped
+                a[0] = (v[1] + v[5]) >> 1; a[1] = (v[3] + v[5]) >> 1; a[2] = v[5]; a[3] = v[7];
+                b[0] = (v[0] + v[4]) >> 1; b[1] = (v[2] + v[4]) >> 1; b[2] = v[4]; b[3] = v[6];
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                o.e0[c] |= static_cast<uint32_t>(a[c]) << (8 * q);
+                o.e1[c] |= static_cast<uint32_t>(b[c]) << (8 * q);
+            }
+        }
+    }
+    if (parts > 1) o.pat = __ldg(&T.part[footprint_index(4)][parts - 2][(lo >> 13) & 0x3FF][0]);
+    uint64_t s0 = __brevll(hi), s1 = __brevll(lo);
+    mask_u128(s0, s1, mode_wbits(me));
+    weight_codes(s0, s1, mode_wq(me), 16, codes, nt);
+}
+
+// UNORM16 value of channel c of texel t of a fast / constant RGBA block.
+__device__ __forceinline__ uint32_t rgba_c16(const RgbaOut& o, const uint8_t* codes, int nt, int t, int c) {
+    if (o.cst) return o.c16[c];
+    const uint32_t part = (o.pat >> (2 * t)) & 3u;
+    const uint32_t w = __ldg(o.wun + codes[t * nt]);
+    const uint32_t X = ((o.e0[c] >> (8 * part)) & 0xFFu) * (64u - w) + ((o.e1[c] >> (8 * part)) & 0xFFu) * w;
+    return 4u * X + ((X + 32u) >> 6);
+}
+
 }  // namespace fast
 }  // namespace akv

@@ -48,8 +48,9 @@ def oracle_restore(blocks, offsets, scales, normalization, block, layout, dim, p
             + offsets.reshape(H, pages, 1, dim).astype(np.float32)
         return r.reshape(H, T, dim).astype(np.float32)
     if normalization == "block_affine":
-        s = np.repeat(np.repeat(scales.astype(np.float32), block, 1), block, 2)[:, :T, :dim]
-        o = np.repeat(np.repeat(offsets.astype(np.float32), block, 1), block, 2)[:, :T, :dim]
+        bw = block * (4 if layout == "rgba" else 1)  # channels one block spans
+        s = np.repeat(np.repeat(scales.astype(np.float32), block, 1), bw, 2)[:, :T, :dim]
+        o = np.repeat(np.repeat(offsets.astype(np.float32), block, 1), bw, 2)[:, :T, :dim]
         return (u * s + o).astype(np.float32)
     raise ValueError(normalization)
 

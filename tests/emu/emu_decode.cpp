@@ -136,3 +136,39 @@ extern "C" int emu_decode_fast_r(const uint8_t* blocks, int64_t n, int bs, float
     }
     return 0;
 }
+
+// The attention kernel's RGBA 4x4 path: block kind, then the fast / constant
+// decode (fp16-view values of all four channels per texel, out[n][16][4]), or
+// the generic decoder for other blocks, as the kernel's in-thread fallback.
+extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, int* cls) {
+    static bool ready = false;
+    if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
+    namespace F = akv::fast;
+    for (int64_t i = 0; i < n; ++i) {
+        uint4 b;
+        std::memcpy(&b, blocks + 16 * i, 16);
+        uint32_t me;
+        int cq;
+        const int kind = F::rgba_block_kind(b, me, cq);
+        cls[i] = kind;
+        float* o = out + i * 64;
+        if (kind == F::kKindGeneric) {
+            akv::BlockDesc<4> d;
+            uint8_t w[64];
+            akv::decode_header<4>(b, akv::footprint_index(4), d, w);
+            for (int t = 0; t < 16; ++t) {
+                uint32_t c[4];
+                akv::texel_values<4, 4>(d, w, t & 3, t >> 2, c);
+                for (int k = 0; k < 4; ++k) o[4 * t + k] = akv::c16_to_unit(c[k]);
+            }
+            continue;
+        }
+        uint8_t codes[16 + F::kCodePad];
+        std::memset(codes, 0xEE, sizeof(codes));
+        F::RgbaOut r;
+        F::decode_rgba4(b, kind, me, cq, codes, 1, r);
+        for (int t = 0; t < 16; ++t)
+            for (int k = 0; k < 4; ++k) o[4 * t + k] = akv::c16_to_unit(F::rgba_c16(r, codes, 1, t, k));
+    }
+    return 0;
+}

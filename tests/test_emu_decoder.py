@@ -92,3 +92,28 @@ def test_fast_table_decode_matches_oracle(source, bs):
     # generic kind (kKindGeneric = 2).
     assert (cls <= 1).any() if source != "garbage" else ((cls == 3).any() and (cls == 2).any())
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("source", ["random", "garbage", "encoder"])
+def test_rgba4_fast_decode_matches_oracle(source):
+    """The attention kernel's RGBA 4x4 path (fast blocks: one plane, full
+    grid, <= 2 partitions, RGBA-direct endpoints; constants; generic
+    fallback) against the oracle's fp16 view of all four channels."""
+    from astc_kv_cuda.ops import host_encode, random_blocks
+    if source == "random":
+        blocks = random_blocks(20000, 4, seed=91)
+    elif source == "garbage":
+        blocks = np.random.default_rng(92).integers(0, 256, (20000, 16), dtype=np.uint8)
+    else:
+        x = np.random.default_rng(93).random((4 * 20, 4 * 22, 4), np.float32)
+        blocks = np.frombuffer(host_encode(x, 4, "rgba", 1), np.uint8).reshape(-1, 16)
+    lib = ct.CDLL(str(EMU))
+    lib.emu_decode_rgba4.argtypes = [ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 16)
+    got = np.empty((b.shape[0], 16, 4), np.float32)
+    cls = np.empty(b.shape[0], np.int32)
+    assert lib.emu_decode_rgba4(b.ctypes.data, b.shape[0], got.ctypes.data, cls.ctypes.data) == 0
+    ref = O.decode_blocks(b, 4, O.OUT_FP16, threads=4).reshape(b.shape[0], 16, 4).astype(np.float32)
+    if source == "encoder":
+        assert (cls == 0).mean() > 0.9  # the encoder's RGBA blocks take the fast path
+    np.testing.assert_array_equal(got, ref)

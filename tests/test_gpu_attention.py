@@ -221,41 +221,39 @@ def test_invalid_descriptors_return_status(cuda):
     assert e.value.code == 2
 
 
-@pytest.mark.parametrize("block,D,G", [(6, 128, 4), (4, 128, 4), (8, 128, 8), (6, 64, 3)])
-@pytest.mark.parametrize("norm", ["block_affine", "token"])
-def test_fused_kernel_on_every_block_mode(cuda, block, D, G, norm):
+@pytest.mark.parametrize("block,D,G,layout,P", [(6, 128, 4, "scalar", 96), (4, 128, 4, "scalar", 64),
+                                                 (8, 128, 8, "scalar", 64), (6, 64, 3, "scalar", 96),
+                                                 (4, 64, 3, "rgba", 16), (4, 128, 4, "rgba", 64)])
+@pytest.mark.parametrize("norm", ["block_affine", "token", "page_channel"])
+def test_fused_kernel_on_every_block_mode(cuda, block, D, G, layout, P, norm):
     """V planes of random legal LDR blocks (every block mode, endpoint mode,
     partition count, dual plane, void extent) mixed with illegal encodings,
-    through the fused kernel's table / direct / descriptor / generic paths,
+    through the fused kernel's table / direct / descriptor / generic paths
+    (scalar and RGBA layouts; 16-token RGBA pages put four pages in a chunk),
     against the oracle decode + restore + float64 attention."""
     from astc_kv_cuda.ops import Attention, contiguous_astc_plane, contiguous_fp16_plane, random_blocks
-    from astc_kv_cuda import _lib as L
-    rng = np.random.default_rng(block * 100 + D + (norm == "token"))
+    rng = np.random.default_rng(block * 100 + D + len(norm) + len(layout))
     B, Hkv = 2, 2
     Hq = Hkv * G
-    P = {4: 64, 6: 96, 8: 64}[block]
-    T = 2 * P
-    rows, cols = T // block, -(-D // block)
+    T = 128 if P == 16 else 2 * P
+    rows, cols = T // block, (D // (4 * block) if layout == "rgba" else -(-D // block))
     n = B * Hkv * rows * cols
     blk = random_blocks(n, block, seed=7 + block)
     bad = rng.random(n) < 0.05  # sprinkle illegal byte patterns (error colour)
     blk[bad] = rng.integers(0, 256, (int(bad.sum()), 16), dtype=np.uint8)
     blocks = blk.reshape(B, Hkv, rows, cols, 16)
-    if norm == "block_affine":
-        off = (rng.standard_normal((B, Hkv, rows, cols)) * 0.5).astype(np.float16)
-        scl = (rng.random((B, Hkv, rows, cols)) * 3 + 0.25).astype(np.float16)
-    else:
-        off = (rng.standard_normal((B, Hkv, T)) * 0.5).astype(np.float16)
-        scl = (rng.random((B, Hkv, T)) * 3 + 0.25).astype(np.float16)
-    vr = np.stack([oracle_restore(blocks[b], off[b], scl[b], norm, block, "scalar", D, P) for b in range(B)])
+    meta_shape = {"block_affine": (B, Hkv, rows, cols), "token": (B, Hkv, T), "page_channel": (B, Hkv, T // P, D)}[norm]
+    off = (rng.standard_normal(meta_shape) * 0.5).astype(np.float16)
+    scl = (rng.random(meta_shape) * 3 + 0.25).astype(np.float16)
+    vr = np.stack([oracle_restore(blocks[b], off[b], scl[b], norm, block, layout, D, P) for b in range(B)])
     k = (rng.standard_normal((B, Hkv, T, D)) * 0.7).astype(np.float16)
     q = rng.standard_normal((B, Hq, D)).astype(np.float32)
     lens = [T, T - 7]
-    vp = contiguous_astc_plane(torch.from_numpy(blocks).cuda(), f16t(off), f16t(scl), block=block, layout="scalar",
+    vp = contiguous_astc_plane(torch.from_numpy(blocks).cuda(), f16t(off), f16t(scl), block=block, layout=layout,
                                normalization=norm, head_dim=D, page_tokens=P)
     attn = Attention(torch.from_numpy(q).cuda(), contiguous_fp16_plane(f16t(k), P), vp, page_tokens=P, max_tokens=T,
                      seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"))
     assert attn.plan()["kernel"] == "attn_fast_kernel"
     got = attn.run().cpu().numpy()
     ref = O.attention_f64(q, k.astype(np.float32), vr, lens)
-    assert_attention_close(got, ref, f"every-mode {block}x{block} {norm} D{D}")
+    assert_attention_close(got, ref, f"every-mode {layout} {block}x{block} {norm} D{D} P{P}")
