@@ -96,6 +96,16 @@ def astc_width(head_dim: int, layout: str, block: int) -> int:
     return (head_dim // comp + block - 1) // block * block
 
 
+def _check_meta(offsets: torch.Tensor, scales: torch.Tensor) -> None:
+    """Plane metadata must be finite fp16 (a NaN/inf scale or offset would
+    poison every attention output that reads the block); checked once when
+    the plane is built, not per step."""
+    if offsets.dtype != torch.float16 or scales.dtype != torch.float16:
+        raise ValueError("plane metadata must be fp16")
+    if not bool(torch.isfinite(offsets).all()) or not bool(torch.isfinite(scales).all()):
+        raise ValueError("non-finite plane metadata (offsets / scales)")
+
+
 def contiguous_astc_plane(blocks: torch.Tensor, offsets: torch.Tensor, scales: torch.Tensor, *, block: int,
                           layout: str, normalization: str, head_dim: int, page_tokens: int,
                           side: torch.Tensor | None = None, side_channels: torch.Tensor | None = None) -> DevicePlane:
@@ -105,6 +115,7 @@ def contiguous_astc_plane(blocks: torch.Tensor, offsets: torch.Tensor, scales: t
     Optional side plane [B, H, T, S] fp16 with channel ids [H, S] int32."""
     B, H, rows, cols, sixteen = blocks.shape
     assert sixteen == 16 and blocks.dtype == torch.uint8
+    _check_meta(offsets, scales)
     T = rows * block
     if T % page_tokens or page_tokens % block:
         raise ValueError("tokens must be whole pages and pages whole block rows")
@@ -147,6 +158,7 @@ def paged_astc_plane(atlas: torch.Tensor, offsets: torch.Tensor, scales: torch.T
     block table passed to `decode_attention`."""
     P, H, prow, cols, sixteen = atlas.shape
     assert sixteen == 16 and prow * block == page_tokens
+    _check_meta(offsets, scales)
     page_bytes = prow * cols * 16
     mp = offsets[0, 0].numel()
     return DevicePlane("astc", atlas, 0, page_bytes, H * page_bytes, block=block, layout=layout,

@@ -95,3 +95,22 @@ def test_random_blocks_are_legal_and_cover_modes():
     assert {i["partitions"] for i in infos if i["kind"] == 0} == {1, 2, 3, 4}
     assert any(i["dual"] for i in infos)
     assert any(i["kind"] == 2 for i in infos)
+
+
+def test_non_finite_plane_metadata_is_rejected():
+    """Failure detection on the host: NaN / inf scales or offsets are refused
+    when a device plane is built (before any launch)."""
+    import torch
+    from astc_kv_cuda.ops import contiguous_astc_plane, paged_astc_plane
+    blocks = torch.zeros((1, 1, 16, 22, 16), dtype=torch.uint8)
+    good = torch.ones((1, 1, 16, 22), dtype=torch.float16)
+    for bad_value in (float("nan"), float("inf")):
+        bad = good.clone()
+        bad[0, 0, 3, 5] = bad_value
+        for off, scl in ((bad, good), (good, bad)):
+            with pytest.raises(ValueError, match="non-finite"):
+                contiguous_astc_plane(blocks, off, scl, block=6, layout="scalar", normalization="block_affine",
+                                      head_dim=128, page_tokens=96)
+            with pytest.raises(ValueError, match="non-finite"):
+                paged_astc_plane(blocks[0][:, None], off[0][:, None], scl[0][:, None], block=6, layout="scalar",
+                                 normalization="block_affine", head_dim=128, page_tokens=96)
