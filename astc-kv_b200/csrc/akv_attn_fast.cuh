@@ -281,9 +281,29 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
     const int tid = threadIdx.x;
     if (tid == 0) ds.nslot = 0;
     __syncthreads();
-    for (int i = tid; i < nblk; i += THREADS) {
+    // Work items: when the chunk's 4 x 8 tiles of blocks (block rows x block
+    // columns) fit the scratch columns, lane l of item group g takes block
+    // (4 tr + l / 8, 8 tc + l % 8) of tile g, so the lanes' pair stores into
+    // the tiles fall on distinct banks (6x6: row offsets 24 banks, column
+    // offsets 3); otherwise items are blocks in row-major order. Either way
+    // a thread's scratch column is its thread index.
+    constexpr int NC = DecodeScratch<NB, THREADS, BS>::NC;
+    const int tiles_c = (cols + 7) >> 3, ntiles = ((rows_blk + 3) >> 2) * tiles_c;
+    const bool tiled = ntiles * 32 <= NC;
+    const int nitems = tiled ? ntiles * 32 : nblk;
+    for (int it = tid; it < nitems; it += THREADS) {
+        int br, bc;
+        if (tiled) {
+            const int tile = it >> 5, tr = tile / tiles_c, tc = tile - tr * tiles_c;
+            br = 4 * tr + ((it >> 3) & 3);
+            bc = 8 * tc + (it & 7);
+            if (br >= rows_blk || bc >= cols) continue;
+        } else {
+            br = it / cols;
+            bc = it - br * cols;
+        }
+        const int i = br * cols + bc;
         const uint4 blk = raw[i];
-        const int br = i / cols, bc = i - br * cols;
         const int row0 = br * BS, col0 = bc * BS;
         const int rows = valid ? min(BS, n - row0) : 0;
         const int ncol = min(BS, D - col0);
@@ -306,7 +326,6 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
             }
         }
         LumOut o;
-        constexpr int NC = DecodeScratch<NB, THREADS, BS>::NC;
         decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], NC,
                        slot >= 0 ? &ds.desc[slot] : nullptr, slot >= 0 ? ds.w[slot] : nullptr, o);
         if (slot < 0)
