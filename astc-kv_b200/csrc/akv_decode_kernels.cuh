@@ -6,12 +6,12 @@
 namespace akv {
 
 constexpr int kDecodeThreads = 256;
-constexpr int kDecodeBlocksPerIter = 128;
+constexpr int kDecodeBlocksPerIter = 256;  // one header per thread: no warp idles in stage A
 
 // Persistent grid-stride decode of consecutive blocks into
-// out[block][y][x][rgba]. Stage A decodes 128 headers into shared memory,
-// stage B evaluates every texel with consecutive threads on consecutive
-// texels so the output stores coalesce.
+// out[block][y][x][rgba]. Stage A decodes 256 headers into shared memory
+// (one per thread), stage B evaluates every texel with consecutive threads
+// on consecutive texels so the output stores coalesce.
 template <int BS, int MODE>
 __global__ void __launch_bounds__(kDecodeThreads) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
                                                                        void* __restrict__ out) {
