@@ -313,7 +313,7 @@ class Workload:
                          "v_blocks": "this library's encoder (astcenc absent)", "split": "64 x 128"}
             split = 128
         elif name == "c3":
-            B, Hq, Hkv, D, T, P = 8, 64, 8, 128, 131072, 64
+            B, Hq, Hkv, D, T, P = batch or 8, 64, 8, 128, 131072, 64
             kcols, vcols = 32, 16
             kpool = torch.from_numpy(encoder_pool(4, "scalar", D, 4096, 2)).to(device)
             vpool = torch.from_numpy(encoder_pool(8, "scalar", D, 2048, 3)).to(device)
