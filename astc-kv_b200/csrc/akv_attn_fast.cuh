@@ -191,10 +191,50 @@ struct DecodeScratch {
     uint32_t tab[kTabCap<BS> > 0 ? kTabCap<BS> : 1][NC];  // value tables, thread-interleaved (conflict-free lookups)
     uint8_t codes[N + kCodePad][NC];  // weight codes, thread-interleaved (+ slack rows)
     int nslot;                  // descriptor slots taken in this plane-chunk
-    uint16_t slow_blk[kSlowCap];
+    // Per slot: tile row | kSlotRows | tile column << 16; block-affine
+    // (scale, offset); owner thread | weight range << 16 (late expansion).
+    uint32_t slot_pos[kSlowCap];
+    float2 slot_aff[kSlowCap];
+    uint32_t slot_src[kSlowCap];
     BlockDesc<1> desc[kSlowCap];
-    uint8_t w[kSlowCap][72];    // grid weights (+ 8 bytes of slack for the infill taps)
+    // Grid weights: rows of 8 bytes for luminance descriptors (desc_seg_c16),
+    // the decode_header layout for generic blocks; 8 bytes of slack either way.
+    alignas(16) uint8_t w[kSlowCap][72];
 };
+
+// Slot flag: a luminance descriptor (decode_lum) evaluated by desc_seg_c16.
+constexpr uint32_t kSlotRows = 1u << 15;
+
+// One texel value v (fp32) -> the hi/lo tiles.
+template <int LD>
+__device__ __forceinline__ void put_texel(float v, bool ok, int row, int col, __half (*thi)[LD], __half (*tlo)[LD]) {
+    const __half hv = __float2half_rn(v);
+    thi[row][col] = ok ? hv : __float2half_rn(0.f);
+    tlo[row][col] = ok ? __float2half_rn(v - __half2float(hv)) : __float2half_rn(0.f);
+}
+
+// Texel row y of a generic slot (decode_header layout) -> the hi/lo tiles
+// (out of line: generic blocks are rare).
+template <int BS, int D, int LD>
+__device__ __noinline__ void eval_row_generic(const BlockDesc<1>& d, const uint8_t* w, int y, int row, int col0,
+                                              bool ok, int norm, float2 aff, const __half* moff, const __half* mscl,
+                                              __half (*thi)[LD], __half (*tlo)[LD]) {
+    const bool lean = !(d.info & ((1u << kInfoVoid) | (1u << kInfoError) | (1u << kInfoDual)));
+    for (int x = 0; x < BS && col0 + x < D; ++x) {
+        uint32_t c16;
+        if (lean) {
+            c16 = desc_texel_c16<BS>(d, w, y * BS + x);
+        } else {
+            uint32_t cv[1];
+            texel_values<BS, 1>(d, w, x, y, cv);
+            c16 = cv[0];
+        }
+        float s = aff.x, o = aff.y;
+        if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row]); o = __half2float(moff[row]); }
+        if (norm == AKV_NORM_PAGE_CHANNEL) { s = __half2float(mscl[col0 + x]); o = __half2float(moff[col0 + x]); }
+        put_texel<LD>(fmaf(c16_to_unit(c16), s, o), ok, row, col0 + x, thi, tlo);
+    }
+}
 
 // Texels of one table / constant block -> the hi/lo tiles (pairs of columns
 // per 32-bit store), from the value table or, for kDirect footprints, from
@@ -257,24 +297,18 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
     }
 }
 
-// One texel value v (fp32) -> the hi/lo tiles.
-template <int LD>
-__device__ __forceinline__ void put_texel(float v, bool ok, int row, int col, __half (*thi)[LD], __half (*tlo)[LD]) {
-    const __half hv = __float2half_rn(v);
-    thi[row][col] = ok ? hv : __float2half_rn(0.f);
-    tlo[row][col] = ok ? __float2half_rn(v - __half2float(hv)) : __float2half_rn(0.f);
-}
-
 // Decode one plane's chunk into the hi/lo tiles. All threads call it.
 //   phase 1  thread per block: table and constant blocks go straight to the
 //            tiles; descriptor and generic blocks take a scratch slot;
-//   phase 1b thread per texel of the slotted blocks.
+//   phase 1a thread per grid-weight row of the descriptor slots (when each
+//            thread decoded at most one block);
+//   phase 1b thread per texel row (6x6: texel pair) of the slotted blocks.
 template <int BS, int D, int THREADS, int NB, int LD>
 __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* moff, const __half* mscl, int norm,
                                              int cols, int rows_blk, int n, bool valid,
                                              DecodeScratch<NB, THREADS, BS>& ds, __half (*thi)[LD],
                                              __half (*tlo)[LD]) {
-    constexpr int N = BS * BS;
+    static_assert(BS % 2 == 0 && D % 8 == 0, "texel pairs; whole 8-texel rows");
     constexpr int kCap = DecodeScratch<NB, THREADS, BS>::kSlowCap;
     const int nblk = rows_blk * cols;
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
@@ -291,6 +325,11 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
     const int tiles_c = (cols + 7) >> 3, ntiles = ((rows_blk + 3) >> 2) * tiles_c;
     const bool tiled = ntiles * 32 <= NC;
     const int nitems = tiled ? ntiles * 32 : nblk;
+    // With at most one block per thread the code columns survive phase 1, so
+    // descriptor grid weights are expanded by all threads afterwards (a lane
+    // expanding its block alone would hold up its warp); otherwise by the
+    // owner right away.
+    const bool late_w = nitems <= THREADS;
     for (int it = tid; it < nitems; it += THREADS) {
         int br, bc;
         if (tiled) {
@@ -319,7 +358,9 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
                 eval_block_generic<BS, LD>(blk, norm, sc, of, moff, mscl, row0, col0, rows, ncol, thi, tlo);
                 continue;
             }
-            ds.slow_blk[slot] = static_cast<uint16_t>(i);
+            ds.slot_pos[slot] = static_cast<uint32_t>(row0) | (static_cast<uint32_t>(col0) << 16) |
+                                (kind == kKindDesc ? kSlotRows : 0u);
+            ds.slot_aff[slot] = make_float2(sc, of);
             if (kind == kKindGeneric) {
                 decode_header_slow<BS>(blk, ds.desc[slot], ds.w[slot]);
                 continue;
@@ -327,38 +368,92 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
         }
         LumOut o;
         decode_lum<BS>(blk, kind, me, cq, affine, sc, of, &ds.tab[0][tid], &ds.codes[0][tid], NC,
-                       slot >= 0 ? &ds.desc[slot] : nullptr, slot >= 0 ? ds.w[slot] : nullptr, o);
-        if (slot < 0)
+                       slot >= 0 ? &ds.desc[slot] : nullptr, o);
+        if (slot < 0) {
             write_block<BS, LD>(o, &ds.tab[0][tid], &ds.codes[0][tid], NC, norm, sc, of, moff, mscl, row0, col0,
                                 rows, ncol, thi, tlo);
+        } else if (late_w) {
+            ds.slot_src[slot] = static_cast<uint32_t>(tid) | (static_cast<uint32_t>(mode_wq(me)) << 16);
+        } else {
+            const uint8_t* un = g_akv_tables.wunq[mode_wq(me)];
+            const int wx = mode_wx(me), wy = mode_wy(me);
+            for (int r = 0; r < wy; ++r) {
+#pragma unroll
+                for (int c = 0; c < BS; ++c)
+                    if (c < wx) ds.w[slot][8 * r + c] = desc_weight(&ds.codes[0][tid], NC, un, wx, 8 * r + c);
+            }
+        }
     }
     __syncthreads();
     const int nslow = min(ds.nslot, kCap);
     if (nslow > 0) {
-        // Phase 1b: texels of the slotted blocks.
-        const int ntex = nslow * N;
-        for (int task = tid; task < ntex; task += THREADS) {
-            const int slot = task / N, t = task - slot * N;
-            const int i = ds.slow_blk[slot];
-            const int x = t % BS, y = t / BS;
-            const int br = i / cols, bc = i - br * cols;
-            const int row = br * BS + y, col = bc * BS + x;
-            if (col >= D) continue;
-            const BlockDesc<1>& d = ds.desc[slot];
-            uint32_t c16;
-            if (d.info & ((1u << kInfoVoid) | (1u << kInfoError) | (1u << kInfoDual))) {
-                uint32_t cv[1];
-                texel_values<BS, 1>(d, ds.w[slot], x, y, cv);
-                c16 = cv[0];
-            } else {
-                c16 = desc_texel_c16<BS>(d, ds.w[slot], t);
+        if (late_w) {
+            // Phase 1a: grid weights of the descriptor slots, one grid row per
+            // task.
+            for (int task = tid; task < nslow * 8; task += THREADS) {
+                const int slot = task >> 3, r = task & 7;
+                if (!(ds.slot_pos[slot] & kSlotRows)) continue;
+                const uint32_t info = ds.desc[slot].info, src = ds.slot_src[slot];
+                const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
+                if (r >= wy) continue;
+                const uint8_t* un = g_akv_tables.wunq[src >> 16];
+                const uint8_t* cc = &ds.codes[0][src & 0xFFFFu];
+#pragma unroll
+                for (int c = 0; c < BS; ++c)
+                    if (c < wx) ds.w[slot][8 * r + c] = desc_weight(cc, NC, un, wx, 8 * r + c);
             }
-            const float u = c16_to_unit(c16);
-            float s, o;
-            if (affine) { s = __half2float(mscl[i]); o = __half2float(moff[i]); }
-            else if (norm == AKV_NORM_TOKEN) { s = __half2float(mscl[row]); o = __half2float(moff[row]); }
-            else { s = __half2float(mscl[col]); o = __half2float(moff[col]); }
-            put_texel<LD>(fmaf(u, s, o), valid && row < n, row, col, thi, tlo);
+            __syncthreads();
+        }
+        // Phase 1b: one segment (kDescSeg texels of a row) of a slotted block
+        // per task; generic slots take a whole row per segment-0 task.
+        constexpr int SEG = kDescSeg<BS>;
+        constexpr int NSEG = BS / SEG;
+        const int ntask = nslow * BS * NSEG;
+        for (int task = tid; task < ntask; task += THREADS) {
+            const int slot = task / (BS * NSEG), r = task - slot * (BS * NSEG);
+            const int y = r / NSEG, x0 = (r - y * NSEG) * SEG;
+            const uint32_t pos = ds.slot_pos[slot];
+            const int row = static_cast<int>(pos & 0x7FFFu) + y, col0 = static_cast<int>(pos >> 16);
+            const BlockDesc<1>& d = ds.desc[slot];
+            const bool ok = valid && row < n;
+            const float2 aff = ds.slot_aff[slot];
+            if (!(pos & kSlotRows)) {
+                if (x0 == 0)
+                    eval_row_generic<BS, D, LD>(d, ds.w[slot], y, row, col0, ok, norm, aff, moff, mscl, thi, tlo);
+                continue;
+            }
+            const int col = col0 + x0;
+            if (col >= D) continue;
+            uint32_t c[SEG];
+            desc_seg_c16<BS, SEG>(d.info, ds.w[slot],
+                                  row_pattern<BS>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y), d.ep[0], d.ep[1], y,
+                                  x0, c);
+            float rs = aff.x, ro = aff.y;
+            if (norm == AKV_NORM_TOKEN) { rs = __half2float(mscl[row]); ro = __half2float(moff[row]); }
+            uint32_t hw[SEG / 2], lw[SEG / 2];
+#pragma unroll
+            for (int x = 0; x < SEG; x += 2) {
+                float s0 = rs, o0 = ro, s1 = rs, o1 = ro;
+                if (norm == AKV_NORM_PAGE_CHANNEL && col + x < D) {
+                    s0 = __half2float(mscl[col + x]); o0 = __half2float(moff[col + x]);
+                    s1 = __half2float(mscl[col + x + 1]); o1 = __half2float(moff[col + x + 1]);
+                }
+                split_pair(fmaf(c16_to_unit(c[x]), s0, o0), fmaf(c16_to_unit(c[x + 1]), s1, o1), hw[x / 2], lw[x / 2]);
+                if (!ok) hw[x / 2] = lw[x / 2] = 0u;
+            }
+            if constexpr (SEG == 8) {
+                // A whole 8x8 row: one 16-byte store per tile (column 8 bc).
+                *reinterpret_cast<uint4*>(&thi[row][col]) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4*>(&tlo[row][col]) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            } else {
+#pragma unroll
+                for (int x = 0; x < SEG; x += 2) {
+                    if (col + x < D) {
+                        *reinterpret_cast<uint32_t*>(&thi[row][col + x]) = hw[x / 2];
+                        *reinterpret_cast<uint32_t*>(&tlo[row][col + x]) = lw[x / 2];
+                    }
+                }
+            }
         }
         __syncthreads();
     }

@@ -9,8 +9,9 @@
 // a full-resolution grid becomes a value table (entry = partition * levels +
 // weight code, affine and fp16 hi/lo split folded in) plus one weight-code
 // byte per texel; with a reduced grid, or a table larger than kTabCap<BS>, it
-// becomes a descriptor evaluated per texel. Everything else takes the
-// generic decoder of akv_astc_device.cuh.
+// becomes a descriptor evaluated a texel row (or pair) at a time
+// (desc_seg_c16). Everything else takes the generic decoder of
+// akv_astc_device.cuh.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -260,12 +261,13 @@ __device__ __forceinline__ float direct_unit(const LumOut& o, const uint8_t* cod
 
 // Runtime path for table, descriptor and constant blocks (kind from
 // block_kind). Table / constant: tab and codes filled, `o` describes them.
-// Descriptor: *d and w filled as decode_header fills them (codes used as
-// scratch).
+// Descriptor: d's partitions and info filled as decode_header fills them,
+// d->ep[0] / ep[1] = the endpoints e0 / e1 of partitions 0..3 packed as bytes
+// (desc_seg_c16's e0p / e1p), and the weight codes left in codes[j * nt]
+// for desc_weight.
 template <int BS>
 __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int cq, bool affine, float sc, float of,
-                                           uint32_t* tab, uint8_t* codes, int nt, BlockDesc<1>* d, uint8_t* w,
-                                           LumOut& o) {
+                                           uint32_t* tab, uint8_t* codes, int nt, BlockDesc<1>* d, LumOut& o) {
     constexpr int fp = footprint_index(BS);
     constexpr int N = BS * BS;
     const Tables& T = g_akv_tables;
@@ -318,22 +320,22 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
         weight_codes(s0, s1, wq, count, codes, nt);
     }
     if (kind == kKindDesc) {
-        const uint8_t* un = T.wunq[wq];
-        for (int j = 0; j < count; ++j) w[j] = __ldg(un + codes[j * nt]);
         d->pat[0] = o.pat[0];
         d->pat[1] = o.pat[1];
         d->pat_hi[0] = o.pat[2];
         d->pat_hi[1] = o.pat[3];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) d->ep[q] = q < parts ? static_cast<uint32_t>(v[2 * q] | (v[2 * q + 1] << 8)) : 0u;
+        // Endpoints of partitions 0..3 packed as bytes (desc_seg_c16).
+        d->ep[0] = static_cast<uint32_t>(v[0] | (v[2] << 8) | (v[4] << 16) | (v[6] << 24));
+        d->ep[1] = static_cast<uint32_t>(v[1] | (v[3] << 8) | (v[5] << 16) | (v[7] << 24));
         d->info = static_cast<uint32_t>(parts - 1) | ((me & kModeReduced) ? (1u << kInfoReduced) : 0u) |
                   (static_cast<uint32_t>(wx) << kInfoWx) | (static_cast<uint32_t>(wy) << kInfoWy);
     }
 }
 
-// UNORM16 value C of texel t of a single-plane descriptor (what texel_values
-// gives for it) through the host-built infill taps; w must have 8 readable
-// bytes of slack past the grid (taps past the grid carry weight 0).
+// UNORM16 value C of texel t of a single-plane descriptor from decode_header
+// (grid weights with a row stride of wx; what texel_values gives for it)
+// through the host-built infill taps; w must have 8 readable bytes of slack
+// past the grid (taps past the grid carry weight 0).
 template <int BS>
 __device__ __forceinline__ uint32_t desc_texel_c16(const BlockDesc<1>& d, const uint8_t* w, int t) {
     constexpr int fp = footprint_index(BS);
@@ -353,6 +355,72 @@ __device__ __forceinline__ uint32_t desc_texel_c16(const BlockDesc<1>& d, const 
     const uint32_t ep = d.ep[(word >> (2 * (t & 15))) & 3u];
     const uint32_t X = (ep & 0xFFu) * (64u - wt) + ((ep >> 8) & 0xFFu) * wt;
     return 4u * X + ((X + 32u) >> 6);
+}
+
+// Unquantised grid weight k = 8 r + c (the row-stride-8 layout desc_seg_c16
+// reads) of a descriptor block, from its weight codes codes[j * nt] with
+// j = r * wx + c; meaningful for c < wx, r < wy.
+__device__ __forceinline__ uint8_t desc_weight(const uint8_t* codes, int nt, const uint8_t* un, int wx, int k) {
+    return __ldg(un + codes[((k >> 3) * wx + (k & 7)) * nt]);
+}
+
+// Partition bits of texel row y (2 bits per texel, texel x at bit 2x) from
+// the four pattern words of a block (texels 0..15, 16..31, 32..47, 48..63).
+template <int BS>
+__device__ __forceinline__ uint32_t row_pattern(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3, int y) {
+    const int b = 2 * BS * y;
+    const int k = b >> 5;
+    const uint32_t lo = k == 0 ? p0 : (k == 1 ? p1 : (k == 2 ? p2 : p3));
+    const uint32_t hi = k == 0 ? p1 : (k == 1 ? p2 : p3);
+    return __funnelshift_r(lo, hi, static_cast<uint32_t>(b & 31));
+}
+
+// Texels per phase-1b task of a luminance descriptor: whole rows, except
+// pairs for 6x6 (6x6 planes have few descriptor blocks per chunk, and short
+// tasks keep that phase's critical path short).
+template <int BS>
+constexpr int kDescSeg = BS == 6 ? 2 : BS;
+
+// UNORM16 values C of texels x0 .. x0 + SEG - 1 of row y (SEG = BS with
+// x0 = 0, or SEG = 2 with x0 even) of a single-plane luminance descriptor
+// block (what texel_values gives for them): info as decode_header fills it,
+// grid weights w in rows of 8 bytes plus one readable slack row, the row's
+// partition bits `prow`, and the endpoints of partitions 0..3 as bytes of
+// e0p / e1p. Infill is separable: the row fixes the two grid rows and the t
+// fraction, each column its two grid columns (one byte permute per grid row)
+// and the s fraction.
+template <int BS, int SEG>
+__device__ __forceinline__ void desc_seg_c16(uint32_t info, const uint8_t* w, uint32_t prow, uint32_t e0p,
+                                             uint32_t e1p, int y, int x0, uint32_t (&c)[SEG]) {
+    static_assert(SEG == BS || SEG == 2, "whole rows or pairs");
+    constexpr int fp = footprint_index(BS);
+    const Tables& T = g_akv_tables;
+    const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
+    const uint32_t ty = __ldg(&T.sep[fp][wy - 2][y]);
+    const uint32_t jt = ty & 15u, ft = ty >> 8;
+    const uint2 r0 = *reinterpret_cast<const uint2*>(w + 8 * jt);
+    const uint2 r1 = *reinterpret_cast<const uint2*>(w + 8 * jt + 8);
+    uint32_t txw[SEG == BS ? 4 : 1];
+    if constexpr (SEG == BS) {
+        const uint4 tx = __ldg(reinterpret_cast<const uint4*>(T.sep[fp][wx - 2]));
+        txw[0] = tx.x; txw[1] = tx.y; txw[2] = tx.z; txw[3] = tx.w;
+    } else {
+        txw[0] = __ldg(reinterpret_cast<const uint32_t*>(T.sep[fp][wx - 2]) + (x0 >> 1));
+    }
+    prow >>= 2 * x0;
+#pragma unroll
+    for (int x = 0; x < SEG; ++x) {
+        const uint32_t e = (txw[x >> 1] >> (16 * (x & 1))) & 0xFFFFu;
+        const uint32_t sel = e & 0xFFu, fs = e >> 8;
+        const uint32_t w11 = (fs * ft + 8u) >> 4;
+        const uint32_t a = __byte_perm(r0.x, r0.y, sel), b = __byte_perm(r1.x, r1.y, sel);
+        const uint32_t wt = ((a & 0xFFu) * (16u - fs - ft + w11) + ((a >> 8) & 0xFFu) * (fs - w11) +
+                             (b & 0xFFu) * (ft - w11) + ((b >> 8) & 0xFFu) * w11 + 8u) >> 4;
+        const uint32_t part = (prow >> (2 * x)) & 3u;
+        const uint32_t e0 = (e0p >> (8 * part)) & 0xFFu, e1 = (e1p >> (8 * part)) & 0xFFu;
+        const uint32_t X = e0 * (64u - wt) + e1 * wt;
+        c[x] = 4u * X + ((X + 32u) >> 6);
+    }
 }
 
 // fp32 value of texel t of a table / constant block (for host-side checks;

@@ -263,7 +263,12 @@ void build_tables(Tables* t) {
                         const int i00 = (gs >> 4) + (gt >> 4) * wx;
                         t->infill[f][wx - 2][wy - 2][y * bs + x] =
                             static_cast<uint16_t>(i00 | ((gs & 15) << 6) | ((gt & 15) << 10));
-                    }
+                    }        for (int n = 2; n <= bs; ++n)
+            for (int c = 0; c < 8; ++c) {
+                const int g = c < bs ? (ds * c * (n - 1) + 32) >> 6 : 0;
+                const int j = g >> 4;
+                t->sep[f][n - 2][c] = static_cast<uint16_t>(j | ((j + 1 < 7 ? j + 1 : 7) << 4) | ((g & 15) << 8));
+            }
     }
     static const int kBlocks[kNumFootprints] = {4, 6, 8};
     for (int f = 0; f < kNumFootprints; ++f) {

@@ -53,6 +53,13 @@ struct Tables {
     // i00 | fs << 6 | ft << 10. At the last texel row / column the fraction
     // is 0, so the taps past the grid get zero weight.
     uint16_t infill[kNumFootprints][7][7][64];
+    // The same infill, separated by axis (the spec computes the s and t grid
+    // coordinates independently): for footprint f, grid size n in 2..8 and
+    // texel coordinate c, entry = j | min(j + 1, 7) << 4 | frac << 8 with j the
+    // lower grid index and frac the fraction towards j + 1 (0 at the last
+    // coordinate, so the clamped upper tap never carries weight). Rows of 8
+    // entries (16 bytes) so one vector load fetches a whole row.
+    alignas(16) uint16_t sep[kNumFootprints][7][8];
 };
 
 // Fills `t` on the host. Deterministic; no device calls.

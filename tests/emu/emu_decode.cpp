@@ -23,6 +23,14 @@ inline unsigned __funnelshift_r(unsigned lo, unsigned hi, unsigned s) {
     s &= 31;
     return s ? (lo >> s) | (hi << (32 - s)) : lo;
 }
+// Byte permute with plain-copy selector nibbles (0..7), the only form the
+// decoder uses: result byte n = byte (s >> 4n) & 7 of the 8 bytes {hi, lo}.
+inline unsigned __byte_perm(unsigned lo, unsigned hi, unsigned s) {
+    const unsigned long long v = (static_cast<unsigned long long>(hi) << 32) | lo;
+    unsigned r = 0;
+    for (int n = 0; n < 4; ++n) r |= static_cast<unsigned>((v >> (8 * ((s >> (4 * n)) & 7))) & 0xFF) << (8 * n);
+    return r;
+}
 inline float __int_as_float(int i) { float f; std::memcpy(&f, &i, 4); return f; }
 inline int __float_as_int(float f) { int i; std::memcpy(&i, &f, 4); return i; }
 using std::max;
@@ -68,7 +76,8 @@ extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 // (akv_decode_fast.cuh): block kind, then table / constant blocks (value table
 // + weight codes, or per-texel endpoint/weight evaluation for 4x4, read back as
 // the kernel's tile writer reads them) or
-// descriptor blocks (evaluated per texel as the kernel's phase 1b does).
+// descriptor blocks (grid weights expanded, then evaluated a row or pair of
+// texels at a time, as the kernel's phases 1a / 1b do).
 // Generic blocks are evaluated as the kernel's phase 1b does. Returns the
 // fp16-view values of the R channel per texel; `cls` gets the kind.
 template <int BS>
@@ -104,14 +113,26 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
     uint8_t codes[64 + akv::fast::kCodePad];
     std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
     akv::BlockDesc<1> d;
-    uint8_t w[72];
+    alignas(16) uint8_t w[72];
     std::memset(w, 0xEE, sizeof(w));  // stale slack bytes must not matter
     F::LumOut o;
-    F::decode_lum<BS>(b, kind, me, cq, false, 0.f, 0.f, tab, codes, 1, kind == F::kKindDesc ? &d : nullptr, w, o);
+    F::decode_lum<BS>(b, kind, me, cq, false, 0.f, 0.f, tab, codes, 1, kind == F::kKindDesc ? &d : nullptr, o);
+    if (kind == F::kKindDesc) {
+        const int wx = (d.info >> akv::kInfoWx) & 15, wy = (d.info >> akv::kInfoWy) & 15;
+        for (int k = 0; k < 8 * wy; ++k)
+            if ((k & 7) < wx) w[k] = F::desc_weight(codes, 1, akv::g_akv_tables.wunq[akv::mode_wq(me)], wx, k);
+        constexpr int SEG = F::kDescSeg<BS>;
+        for (int y = 0; y < BS; ++y)
+            for (int x0 = 0; x0 < BS; x0 += SEG) {
+                uint32_t c[SEG];
+                F::desc_seg_c16<BS, SEG>(d.info, w, F::row_pattern<BS>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y),
+                                         d.ep[0], d.ep[1], y, x0, c);
+                for (int x = 0; x < SEG; ++x) out[y * BS + x0 + x] = akv::c16_to_unit(c[x]);
+            }
+        return 0;
+    }
     for (int t = 0; t < N; ++t) {
-        if (kind == F::kKindDesc) {
-            out[t] = akv::c16_to_unit(F::desc_texel_c16<BS>(d, w, t));
-        } else if constexpr (F::kDirect<BS>) {
+        if constexpr (F::kDirect<BS>) {
             out[t] = F::direct_unit(o, codes, 1, t);
         } else {
             const uint32_t c = codes[t] & o.cmask;

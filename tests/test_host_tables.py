@@ -28,6 +28,12 @@ def tables():
     t["wunq"] = take(np.uint8, (12, 32))
     t["cquant"] = take(np.uint8, (10, 128))
     t["shape"] = take(np.uint8, (21,))
+    off += off & 1
+    t["dig3"] = take(np.uint16, (384,))
+    t["infill"] = take(np.uint16, (3, 7, 7, 64))
+    off = (off + 15) // 16 * 16
+    t["sep"] = take(np.uint16, (3, 7, 8))
+    assert (off + 15) // 16 * 16 == raw.size
     return t
 
 
@@ -89,3 +95,28 @@ def test_trit_quint_tables_cover_all_digit_tuples():
     quints = {tuple((int(v) >> (3 * j)) & 7 for j in range(3)) for v in t["quint"]}
     assert len(trits) == 243 and all(max(x) <= 2 for x in trits)
     assert len(quints) == 125 and all(max(x) <= 4 for x in quints)
+
+
+def test_separable_infill_matches_texel_taps():
+    """The per-axis taps (row evaluator) compose to the per-texel taps, both
+    follow the spec's grid coordinates, and a full grid maps to itself."""
+    t = tables()
+    for f, bs in enumerate((4, 6, 8)):
+        ds = (1024 + bs // 2) // (bs - 1)
+        for n in range(2, bs + 1):
+            for c in range(bs):
+                g = (ds * c * (n - 1) + 32) >> 6
+                e = int(t["sep"][f, n - 2, c])
+                j, j1, frac = e & 15, (e >> 4) & 15, e >> 8
+                assert (j, frac) == (g >> 4, g & 15)
+                assert j1 == min(j + 1, 7) and j <= n - 1
+                assert frac == 0 or j + 1 <= n - 1  # the upper tap is inside the grid when it has weight
+                if n == bs:
+                    assert (j, frac) == (c, 0)
+        for wx in range(2, bs + 1):
+            for wy in range(2, bs + 1):
+                for y in range(bs):
+                    for x in range(bs):
+                        ex, ey = int(t["sep"][f, wx - 2, x]), int(t["sep"][f, wy - 2, y])
+                        tap = int(t["infill"][f, wx - 2, wy - 2, y * bs + x])
+                        assert tap == ((ex & 15) + (ey & 15) * wx) | ((ex >> 8) << 6) | ((ey >> 8) << 10)
