@@ -389,10 +389,17 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
     if (nslow > 0) {
         if (late_w) {
             // Phase 1a: grid weights of the descriptor slots, one grid row per
-            // task.
-            for (int task = tid; task < nslow * 8; task += THREADS) {
-                const int slot = task >> 3, r = task & 7;
-                if (!(ds.slot_pos[slot] & kSlotRows)) continue;
+            // task. When that takes more than one round anyway, a warp takes
+            // one row of 32 slots, so its lanes read the owners' code columns
+            // side by side (one row of the code scratch) instead of one
+            // column down (a single bank); else a slot's rows are adjacent.
+            const bool wide = nslow * 8 > THREADS;
+            const int nwtask = wide ? ((nslow + 31) & ~31) * 8 : nslow * 8;
+            for (int task = tid; task < nwtask; task += THREADS) {
+                const int g = task >> 5;
+                const int slot = wide ? (((g >> 3) << 5) | (task & 31)) : task >> 3;
+                const int r = wide ? g & 7 : task & 7;
+                if (slot >= nslow || !(ds.slot_pos[slot] & kSlotRows)) continue;
                 const uint32_t info = ds.desc[slot].info, src = ds.slot_src[slot];
                 const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
                 if (r >= wy) continue;
