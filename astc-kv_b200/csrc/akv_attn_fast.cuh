@@ -236,6 +236,65 @@ __device__ __noinline__ void eval_row_generic(const BlockDesc<1>& d, const uint8
     }
 }
 
+// The 2^16 u values tv of a directly evaluated block, normalised (NORM fixed
+// per instantiation) -> the hi/lo tiles; rows at or past `rows` as zeros.
+template <int BS, int LD, int NORM>
+__device__ __forceinline__ void write_direct_n(const float (&tv)[BS * BS], float sc, float of, const __half* moff,
+                                               const __half* mscl, int row0, int col0, int rows, __half (*thi)[LD],
+                                               __half (*tlo)[LD]) {
+    // Scales times 2^-16 (tv is 2^16 u; exact, the FMA still rounds once).
+    float cs[BS], co[BS];
+#pragma unroll
+    for (int x = 0; x < BS; ++x) {
+        cs[x] = NORM == AKV_NORM_PAGE_CHANNEL ? __half2float(mscl[col0 + x]) * 0x1p-16f : sc * 0x1p-16f;
+        co[x] = NORM == AKV_NORM_PAGE_CHANNEL ? __half2float(moff[col0 + x]) : of;
+    }
+#pragma unroll
+    for (int y = 0; y < BS; ++y) {
+        float rs = 0.f, ro = 0.f;
+        if (NORM == AKV_NORM_TOKEN) {
+            rs = __half2float(mscl[row0 + y]) * 0x1p-16f;
+            ro = __half2float(moff[row0 + y]);
+        }
+#pragma unroll
+        for (int x = 0; x < BS; x += 2) {
+            uint32_t h, l;
+            const float s0 = NORM == AKV_NORM_TOKEN ? rs : cs[x], s1 = NORM == AKV_NORM_TOKEN ? rs : cs[x + 1];
+            const float o0 = NORM == AKV_NORM_TOKEN ? ro : co[x], o1 = NORM == AKV_NORM_TOKEN ? ro : co[x + 1];
+            split_pair(fmaf(tv[y * BS + x], s0, o0), fmaf(tv[y * BS + x + 1], s1, o1), h, l);
+            if (y >= rows) { h = 0u; l = 0u; }
+            *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
+            *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
+        }
+    }
+}
+
+// Texels of a directly evaluated (kDirect) table / constant block -> the
+// hi/lo tiles: every texel's value first (the constant case decided once
+// per block), then the block's normalisation applied with its scales and
+// offsets loaded once (the footprint divides the head dimension, so every
+// column is in range).
+template <int BS, int LD>
+__device__ __forceinline__ void write_direct(const LumOut& o, const uint8_t* codes, int nt, int norm, float sc,
+                                             float of, const __half* moff, const __half* mscl, int row0, int col0,
+                                             int rows, __half (*thi)[LD], __half (*tlo)[LD]) {
+    float tv[BS * BS];
+    if (o.cmask) {
+#pragma unroll
+        for (int t = 0; t < BS * BS; ++t) tv[t] = direct_t(o, codes, nt, t);
+    } else {
+        const float ct = o.cu * 65536.f;
+#pragma unroll
+        for (int t = 0; t < BS * BS; ++t) tv[t] = ct;
+    }
+    if (norm == AKV_NORM_TOKEN)
+        write_direct_n<BS, LD, AKV_NORM_TOKEN>(tv, sc, of, moff, mscl, row0, col0, rows, thi, tlo);
+    else if (norm == AKV_NORM_PAGE_CHANNEL)
+        write_direct_n<BS, LD, AKV_NORM_PAGE_CHANNEL>(tv, sc, of, moff, mscl, row0, col0, rows, thi, tlo);
+    else
+        write_direct_n<BS, LD, AKV_NORM_BLOCK_AFFINE>(tv, sc, of, moff, mscl, row0, col0, rows, thi, tlo);
+}
+
 // Texels of one table / constant block -> the hi/lo tiles (pairs of columns
 // per 32-bit store), from the value table or, for kDirect footprints, from
 // endpoints and weights. Rows at or past `rows` are written as zeros.
@@ -244,6 +303,11 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
                                             int norm, float sc, float of, const __half* moff, const __half* mscl,
                                             int row0, int col0, int rows, int cols, __half (*thi)[LD],
                                             __half (*tlo)[LD]) {
+    if constexpr (kDirect<BS>) {
+        static_assert(BS == 4, "direct evaluation is for 4x4 blocks (whole columns: D % 4 == 0)");
+        write_direct<BS, LD>(o, codes, nt, norm, sc, of, moff, mscl, row0, col0, rows, thi, tlo);
+        return;
+    }
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
     const uint32_t L = static_cast<uint32_t>(o.L);
 #pragma unroll
@@ -259,21 +323,6 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
             if (x < cols) {
                 const int i = y * BS + x;
                 uint32_t h, l;
-                if constexpr (kDirect<BS>) {
-                    // Values from endpoints and weights (no table).
-                    const float u0 = direct_unit(o, codes, nt, i), u1 = direct_unit(o, codes, nt, i + 1);
-                    float s0 = sc, o0 = of, s1 = sc, o1 = of;
-                    if (norm == AKV_NORM_TOKEN) { s0 = s1 = rs; o0 = o1 = ro; }
-                    if (norm == AKV_NORM_PAGE_CHANNEL) {
-                        s0 = __half2float(mscl[col0 + x]); o0 = __half2float(moff[col0 + x]);
-                        s1 = __half2float(mscl[col0 + x + 1]); o1 = __half2float(moff[col0 + x + 1]);
-                    }
-                    split_pair(fmaf(u0, s0, o0), fmaf(u1, s1, o1), h, l);
-                    if (!rok) { h = 0u; l = 0u; }
-                    *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
-                    *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
-                    continue;
-                }
                 const uint32_t c0 = codes[i * nt] & o.cmask, c1 = codes[(i + 1) * nt] & o.cmask;
                 const uint32_t p0 = (o.pat[i >> 4] >> (2 * (i & 15))) & 3u;
                 const uint32_t p1 = (o.pat[(i + 1) >> 4] >> (2 * ((i + 1) & 15))) & 3u;

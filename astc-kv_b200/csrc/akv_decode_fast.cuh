@@ -244,19 +244,21 @@ struct LumOut {
     float cu;
 };
 
-// Unit value u (exact fp16 view as float) of a texel with 8-bit endpoints
-// e0, e1 and weight w (0..64).
-__device__ __forceinline__ float lerp_unit(uint32_t e0, uint32_t e1, uint32_t w) {
+// Texel t of a directly evaluated, non-constant block as 2^16 times its unit
+// value: the fp16 view of C (C truncated to 11 significant bits, 65535 ->
+// 65536) as an integer-valued float. The partition's endpoint bytes come out
+// of e0p / e1p by one byte permute each (selector nibbles 4 pick zero bytes).
+__device__ __forceinline__ float direct_t(const LumOut& o, const uint8_t* codes, int nt, int t) {
+    const uint32_t sel = ((o.pat[t >> 4] >> (2 * (t & 15))) & 3u) | 0x4440u;
+    const uint32_t e0 = __byte_perm(o.e0p, 0u, sel), e1 = __byte_perm(o.e1p, 0u, sel);
+    const uint32_t w = __ldg(o.wun + codes[t * nt]);
     const uint32_t c = (257u * (e0 * (64u - w) + e1 * w) + 32u) >> 6;
-    return __int_as_float(__float_as_int(static_cast<float>(c + (c == 0xFFFFu))) & 0xFFFFE000) * 0x1p-16f;
+    return __int_as_float(__float_as_int(static_cast<float>(c + (c == 0xFFFFu))) & 0xFFFFE000);
 }
 
 // Unit value of texel t of a directly evaluated block.
 __device__ __forceinline__ float direct_unit(const LumOut& o, const uint8_t* codes, int nt, int t) {
-    if (!o.cmask) return o.cu;
-    const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
-    const uint32_t w = __ldg(o.wun + codes[t * nt]);
-    return lerp_unit((o.e0p >> (8 * part)) & 0xFFu, (o.e1p >> (8 * part)) & 0xFFu, w);
+    return o.cmask ? direct_t(o, codes, nt, t) * 0x1p-16f : o.cu;
 }
 
 // Runtime path for table, descriptor and constant blocks (kind from
