@@ -369,6 +369,87 @@ __device__ __forceinline__ void texel_values(const BlockDesc<NCH>& d, const uint
     }
 }
 
+// Partition bits of texel row y (2 bits per texel, texel x at bit 2x) from
+// the four pattern words of a block (texels 0..15, 16..31, 32..47, 48..63).
+template <int BS>
+__device__ __forceinline__ uint32_t row_pattern(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3, int y) {
+    const int b = 2 * BS * y;
+    const int k = b >> 5;
+    const uint32_t lo = k == 0 ? p0 : (k == 1 ? p1 : (k == 2 ? p2 : p3));
+    const uint32_t hi = k == 0 ? p1 : (k == 1 ? p2 : p3);
+    return __funnelshift_r(lo, hi, static_cast<uint32_t>(b & 31));
+}
+
+// Stage B by rows: the 16-bit values C of the BS texels of row y for the NCH
+// channels (out[x][c]), each equal to what texel_values gives for that
+// texel. The row's partition bits and, for a reduced grid, its grid row and
+// t fraction are found once; the per-axis tap table Tables::sep gives the
+// column taps (the spec computes the s and t grid coordinates separately).
+template <int BS, int NCH>
+__device__ __forceinline__ void texel_row(const BlockDesc<NCH>& d, const uint8_t* w, int y,
+                                          uint32_t (&out)[BS][NCH]) {
+    constexpr int fp = footprint_index(BS);
+    const uint32_t info = d.info;
+    if (info & (1u << kInfoVoid)) {
+#pragma unroll
+        for (int x = 0; x < BS; ++x)
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) out[x][c] = d.ep[c];
+        return;
+    }
+    const uint32_t prow = (info & 3u) ? row_pattern<BS>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y) : 0u;
+    const int dual = (info >> kInfoDual) & 1;
+    const int ccs = (info >> kInfoCcs) & 3;
+    const bool err = (info >> kInfoError) & 1;
+    const bool red = (info >> kInfoReduced) & 1;
+    const int wx = (info >> kInfoWx) & 15, wy = (info >> kInfoWy) & 15;
+    int jt = y, ft = 0;
+    uint32_t tx[4] = {0u, 0u, 0u, 0u};
+    if (red && !err) {
+        const uint32_t e = __ldg(&g_akv_tables.sep[fp][wy - 2][y]);
+        jt = static_cast<int>(e & 15u);
+        ft = static_cast<int>(e >> 8);
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(g_akv_tables.sep[fp][wx - 2]));
+        tx[0] = r.x; tx[1] = r.y; tx[2] = r.z; tx[3] = r.w;
+    }
+    const bool has_y = jt + 1 < wy;
+#pragma unroll
+    for (int x = 0; x < BS; ++x) {
+        int wt0 = 0, wt1 = 0;
+        if (err) {
+        } else if (!red) {
+            const int t = y * BS + x;
+            wt0 = w[t << dual];
+            wt1 = dual ? w[(t << 1) + 1] : wt0;
+        } else {
+            const uint32_t e = (tx[x >> 1] >> (16 * (x & 1))) & 0xFFFFu;
+            const int js = static_cast<int>(e & 15u), fs = static_cast<int>(e >> 8);
+            const int w11 = (fs * ft + 8) >> 4;
+            const int f00 = 16 - fs - ft + w11, f01 = fs - w11, f10 = ft - w11;
+            const int i00 = js + jt * wx;
+            const bool has_x = js + 1 < wx;
+#pragma unroll
+            for (int pl = 0; pl < 2; ++pl) {
+                if (pl == 1 && !dual) { wt1 = wt0; break; }
+                const int p00 = w[(i00 << dual) + pl];
+                const int p01 = has_x ? w[((i00 + 1) << dual) + pl] : 0;
+                const int p10 = has_y ? w[((i00 + wx) << dual) + pl] : 0;
+                const int p11 = (has_x && has_y) ? w[((i00 + wx + 1) << dual) + pl] : 0;
+                const int v = (p00 * f00 + p01 * f01 + p10 * f10 + p11 * w11 + 8) >> 4;
+                if (pl == 0) wt0 = v; else wt1 = v;
+            }
+        }
+        const int part = static_cast<int>((prow >> (2 * x)) & 3u);
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const int wt = (dual && ccs == c) ? wt1 : wt0;
+            const uint32_t ep = d.ep[part * NCH + c];
+            const int X = static_cast<int>(ep & 0xFF) * (64 - wt) + static_cast<int>((ep >> 8) & 0xFF) * wt;
+            out[x][c] = static_cast<uint32_t>(4 * X + ((X + 32) >> 6));
+        }
+    }
+}
+
 // fp16 view of C as float (exact): 1.0 for 65535, else C/65536 truncated to 11
 // significant bits.
 __device__ __forceinline__ float c16_to_unit(uint32_t c) {

@@ -343,9 +343,17 @@ int launch_decode(const void* blocks, int64_t n, int mode, void* out, cudaStream
     const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
     const int grid = static_cast<int>(iters < cap ? iters : cap);
     const uint4* b = static_cast<const uint4*>(blocks);
-    if (mode == AKV_OUT_UNORM8) decode_blocks_kernel<BS, AKV_OUT_UNORM8><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
-    else if (mode == AKV_OUT_FP16) decode_blocks_kernel<BS, AKV_OUT_FP16><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
-    else decode_blocks_kernel<BS, AKV_OUT_UNORM16><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    // Vector row stores need a 16-byte aligned output (cudaMalloc'd buffers
+    // are); any other 4-byte aligned output gets the word-store instance.
+    if (reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+        if (mode == AKV_OUT_UNORM8) decode_blocks_kernel<BS, AKV_OUT_UNORM8, true><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+        else if (mode == AKV_OUT_FP16) decode_blocks_kernel<BS, AKV_OUT_FP16, true><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+        else decode_blocks_kernel<BS, AKV_OUT_UNORM16, true><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    } else {
+        if (mode == AKV_OUT_UNORM8) decode_blocks_kernel<BS, AKV_OUT_UNORM8, false><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+        else if (mode == AKV_OUT_FP16) decode_blocks_kernel<BS, AKV_OUT_FP16, false><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+        else decode_blocks_kernel<BS, AKV_OUT_UNORM16, false><<<grid, kDecodeThreads, 0, s>>>(b, n, out);
+    }
     return launch_status();
 }
 

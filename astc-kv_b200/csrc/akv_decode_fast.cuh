@@ -366,17 +366,6 @@ __device__ __forceinline__ uint8_t desc_weight(const uint8_t* codes, int nt, con
     return __ldg(un + codes[((k >> 3) * wx + (k & 7)) * nt]);
 }
 
-// Partition bits of texel row y (2 bits per texel, texel x at bit 2x) from
-// the four pattern words of a block (texels 0..15, 16..31, 32..47, 48..63).
-template <int BS>
-__device__ __forceinline__ uint32_t row_pattern(uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3, int y) {
-    const int b = 2 * BS * y;
-    const int k = b >> 5;
-    const uint32_t lo = k == 0 ? p0 : (k == 1 ? p1 : (k == 2 ? p2 : p3));
-    const uint32_t hi = k == 0 ? p1 : (k == 1 ? p2 : p3);
-    return __funnelshift_r(lo, hi, static_cast<uint32_t>(b & 31));
-}
-
 // Texels per phase-1b task of a luminance descriptor: whole rows, except
 // pairs for 6x6 (6x6 planes have few descriptor blocks per chunk, and short
 // tasks keep that phase's critical path short).

@@ -10,9 +10,11 @@ constexpr int kDecodeBlocksPerIter = 256;  // one header per thread: no warp idl
 
 // Persistent grid-stride decode of consecutive blocks into
 // out[block][y][x][rgba]. Stage A decodes 256 headers into shared memory
-// (one per thread), stage B evaluates every texel with consecutive threads
-// on consecutive texels so the output stores coalesce.
-template <int BS, int MODE>
+// (one per thread); stage B evaluates a texel row per task (texel_row), with
+// consecutive threads on consecutive rows so the output stays contiguous
+// across a warp: with VEC (out 16-byte aligned) each row leaves in 16-byte
+// (8-byte for 6x6 UNORM8) vector stores, else in 32-bit words.
+template <int BS, int MODE, bool VEC>
 __global__ void __launch_bounds__(kDecodeThreads) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
                                                                        void* __restrict__ out) {
     __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
@@ -24,23 +26,39 @@ __global__ void __launch_bounds__(kDecodeThreads) decode_blocks_kernel(const uin
         const int nb = static_cast<int>(min(static_cast<int64_t>(kDecodeBlocksPerIter), n - base));
         if (threadIdx.x < nb) decode_header<4>(__ldg(blocks + base + threadIdx.x), fp, desc[threadIdx.x], wts[threadIdx.x]);
         __syncthreads();
-        const int ntex = nb * TPB;
-        for (int i = threadIdx.x; i < ntex; i += blockDim.x) {
-            const int bi = i / TPB, t = i % TPB;
-            uint32_t c[4];
-            texel_values<BS, 4>(desc[bi], wts[bi], t % BS, t / BS, c);
-            const int64_t o = base * TPB + i;
-            if (MODE == AKV_OUT_UNORM8) {
-                reinterpret_cast<uint32_t*>(out)[o] = (c[0] >> 8) | ((c[1] >> 8) << 8) | ((c[2] >> 8) << 16) | ((c[3] >> 8) << 24);
-            } else if (MODE == AKV_OUT_FP16) {
-                uint2 h;
-                h.x = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[0])))) |
-                      (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[1])))) << 16);
-                h.y = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[2])))) |
-                      (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[3])))) << 16);
-                reinterpret_cast<uint2*>(out)[o] = h;
+        constexpr int WPT = MODE == AKV_OUT_UNORM8 ? 1 : 2;  // 32-bit output words per texel
+        constexpr int NW = BS * WPT;                             // words per texel row
+        for (int r = threadIdx.x; r < nb * BS; r += blockDim.x) {
+            const int bi = r / BS, y = r - bi * BS;
+            uint32_t c[BS][4];
+            texel_row<BS, 4>(desc[bi], wts[bi], y, c);
+            uint32_t pk[NW];
+#pragma unroll
+            for (int x = 0; x < BS; ++x) {
+                if (MODE == AKV_OUT_UNORM8) {
+                    pk[x] = (c[x][0] >> 8) | ((c[x][1] >> 8) << 8) | ((c[x][2] >> 8) << 16) | ((c[x][3] >> 8) << 24);
+                } else if (MODE == AKV_OUT_FP16) {
+                    pk[2 * x] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[x][0])))) |
+                                (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[x][1])))) << 16);
+                    pk[2 * x + 1] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[x][2])))) |
+                                    (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(c16_to_unit(c[x][3])))) << 16);
+                } else {
+                    pk[2 * x] = c[x][0] | (c[x][1] << 16);
+                    pk[2 * x + 1] = c[x][2] | (c[x][3] << 16);
+                }
+            }
+            // First output word of the row: texel (base + bi) * TPB + y * BS.
+            uint32_t* dst = reinterpret_cast<uint32_t*>(out) + ((base + bi) * TPB + y * BS) * WPT;
+            if constexpr (VEC && NW % 4 == 0) {
+#pragma unroll
+                for (int k = 0; k < NW / 4; ++k)
+                    reinterpret_cast<uint4*>(dst)[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+            } else if constexpr (VEC) {
+#pragma unroll
+                for (int k = 0; k < NW / 2; ++k) reinterpret_cast<uint2*>(dst)[k] = make_uint2(pk[2 * k], pk[2 * k + 1]);
             } else {
-                reinterpret_cast<uint2*>(out)[o] = make_uint2(c[0] | (c[1] << 16), c[2] | (c[3] << 16));
+#pragma unroll
+                for (int k = 0; k < NW; ++k) dst[k] = pk[k];
             }
         }
         __syncthreads();

@@ -203,7 +203,7 @@ def run_decode(args) -> dict | None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     import astc_kv_cuda as A
     A.init(local)
-    wl = DecodeWorkload(args.workload, rank, dev)
+    wl = DecodeWorkload(args.workload, rank, dev, args.decode_blocks)
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         wl.run()
@@ -593,6 +593,8 @@ def main():
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "decode4", "decode6", "decode8"], default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling of small cases)")
+    ap.add_argument("--decode-blocks", type=int, default=1 << 26,
+                    help="blocks per step of the decode microbench (a multiple of 2^20; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

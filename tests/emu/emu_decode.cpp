@@ -70,6 +70,38 @@ extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, u
     return 0;
 }
 
+// The standalone decoder's row stage (texel_row): UNORM16 RGBA per texel,
+// out[n][bs][bs][4], as emu_decode_blocks_u16 but a texel row at a time.
+template <int BS>
+static void rows_one(const akv::BlockDesc<4>& d, const uint8_t* w, uint16_t* o) {
+    for (int y = 0; y < BS; ++y) {
+        uint32_t c[BS][4];
+        akv::texel_row<BS, 4>(d, w, y, c);
+        for (int x = 0; x < BS; ++x)
+            for (int k = 0; k < 4; ++k) o[(y * BS + x) * 4 + k] = static_cast<uint16_t>(c[x][k]);
+    }
+}
+
+extern "C" int emu_decode_rows_u16(const uint8_t* blocks, int64_t n, int bs, uint16_t* out) {
+    static bool ready = false;
+    if (!ready) { akv::build_tables(&akv::g_akv_tables); ready = true; }
+    const int fp = akv::footprint_index(bs);
+    if (fp < 0) return 1;
+    for (int64_t i = 0; i < n; ++i) {
+        uint4 b;
+        std::memcpy(&b, blocks + 16 * i, 16);
+        akv::BlockDesc<4> d;
+        uint8_t w[64];
+        std::memset(w, 0xEE, sizeof(w));  // unwritten weights must not matter
+        akv::decode_header<4>(b, fp, d, w);
+        uint16_t* o = out + i * bs * bs * 4;
+        if (bs == 4) rows_one<4>(d, w, o);
+        else if (bs == 6) rows_one<6>(d, w, o);
+        else rows_one<8>(d, w, o);
+    }
+    return 0;
+}
+
 extern "C" float emu_unit(uint32_t c) { return akv::c16_to_unit(c); }
 
 // The per-block runtime path of the attention kernel's plane decode
@@ -125,7 +157,7 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
         for (int y = 0; y < BS; ++y)
             for (int x0 = 0; x0 < BS; x0 += SEG) {
                 uint32_t c[SEG];
-                F::desc_seg_c16<BS, SEG>(d.info, w, F::row_pattern<BS>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y),
+                F::desc_seg_c16<BS, SEG>(d.info, w, akv::row_pattern<BS>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y),
                                          d.ep[0], d.ep[1], y, x0, c);
                 for (int x = 0; x < SEG; ++x) out[y * BS + x0 + x] = akv::c16_to_unit(c[x]);
             }

@@ -40,6 +40,30 @@ def test_random_bytes_including_illegal_encodings(bs):
     np.testing.assert_array_equal(emu_decode(blocks, bs), O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
 
 
+def emu_decode_rows(blocks, bs):
+    lib = ct.CDLL(str(EMU))
+    lib.emu_decode_rows_u16.argtypes = [ct.c_void_p, ct.c_int64, ct.c_int, ct.c_void_p]
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 16)
+    out = np.empty((b.shape[0], bs, bs, 4), np.uint16)
+    assert lib.emu_decode_rows_u16(b.ctypes.data, b.shape[0], bs, out.ctypes.data) == 0
+    return out
+
+
+@pytest.mark.parametrize("bs", [4, 6, 8])
+def test_row_stage_matches_oracle(bs):
+    """The standalone decoder's row-wise texel stage: random legal blocks
+    (every mode: reduced grids, dual plane, 1-4 partitions, void extent),
+    random bytes (illegal encodings -> error colour) and, for 6x6, the
+    reference's astcenc goldens."""
+    from astc_kv_cuda.ops import random_blocks
+    sets = [random_blocks(20000, bs, seed=2000 + bs),
+            np.random.default_rng(50 + bs).integers(0, 256, (20000, 16), dtype=np.uint8)]
+    if bs == 6:
+        sets.append(golden("block_geometry_identity")["blocks"].reshape(-1, 16))
+    for blocks in sets:
+        np.testing.assert_array_equal(emu_decode_rows(blocks, bs), O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
+
+
 def test_fp16_view_conversion_exhaustive():
     lib = ct.CDLL(str(EMU))
     lib.emu_unit.argtypes = [ct.c_uint32]

@@ -110,3 +110,21 @@ def test_restore_plane_bit_exact_block_geometry(cuda):
     for i in range(len(g["names"])):
         rec = _restore(g["blocks"][i].reshape(3, 48, 11, 16), g["offsets"][i], g["scales"][i], "token", 96, 288)
         assert sha(rec) == str(g["decoded_sha256"][i]), str(g["names"][i])
+
+
+@pytest.mark.parametrize("bs", [4, 6, 8])
+@pytest.mark.parametrize("mode,offset", [("unorm8", 4), ("unorm8", 12), ("fp16", 8), ("unorm16", 8)])
+def test_output_not_16_byte_aligned(cuda, bs, mode, offset):
+    """Outputs that are only 4- (UNORM8) or 8-byte aligned take the decoder's
+    word-store instance; results equal the aligned (vector-store) decode."""
+    from astc_kv_cuda.ops import decode_blocks, random_blocks
+    blocks = torch.from_numpy(random_blocks(4099, bs, seed=31 * bs)).cuda()
+    ref = decode_blocks(blocks, bs, mode)
+    nbytes = ref.numel() * ref.element_size()
+    buf = torch.zeros(nbytes + 32, dtype=torch.uint8, device="cuda")
+    assert buf.data_ptr() % 16 == 0
+    out = buf[offset:offset + nbytes].view(ref.dtype).view(ref.shape)
+    decode_blocks(blocks, bs, mode, out=out)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.uint8), ref.view(torch.uint8))
+    assert not buf[:offset].any() and not buf[offset + nbytes:].any()  # nothing written outside
