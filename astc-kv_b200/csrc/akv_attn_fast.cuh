@@ -560,6 +560,41 @@ __device__ __noinline__ void eval_rgba_generic(uint4 blk, int i, int norm, const
     }
 }
 
+// The 16 texels x 4 channels of a fast / constant RGBA 4x4 block -> the
+// hi/lo tiles, with the normalisation NORM fixed per instantiation and its
+// scales (times 2^-16: exact, the FMA still rounds once) and offsets loaded
+// once per texel column (page-channel), row (token) or block (affine).
+template <int LD, int NORM>
+__device__ __forceinline__ void write_rgba_n(const RgbaOut& o, const uint8_t* codes, int nt, int i, const __half* moff,
+                                             const __half* mscl, int row0, int col0, int rows, __half (*thi)[LD],
+                                             __half (*tlo)[LD]) {
+    const float bs = NORM == AKV_NORM_BLOCK_AFFINE ? __half2float(mscl[i]) * 0x1p-16f : 0.f;
+    const float bo = NORM == AKV_NORM_BLOCK_AFFINE ? __half2float(moff[i]) : 0.f;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+        float cs[4], co[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            cs[k] = NORM == AKV_NORM_PAGE_CHANNEL ? __half2float(mscl[col0 + 4 * x + k]) * 0x1p-16f : bs;
+            co[k] = NORM == AKV_NORM_PAGE_CHANNEL ? __half2float(moff[col0 + 4 * x + k]) : bo;
+        }
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+            float tv[4], v[4];
+            rgba_t4(o, codes, nt, 4 * y + x, tv);
+            float rs = 0.f, ro = 0.f;
+            if (NORM == AKV_NORM_TOKEN) {
+                rs = __half2float(mscl[row0 + y]) * 0x1p-16f;
+                ro = __half2float(moff[row0 + y]);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                v[k] = fmaf(tv[k], NORM == AKV_NORM_TOKEN ? rs : cs[k], NORM == AKV_NORM_TOKEN ? ro : co[k]);
+            put_rgba<LD>(v, y < rows, row0 + y, col0 + 4 * x, thi, tlo);
+        }
+    }
+}
+
 // Decode one RGBA 4x4 plane's chunk into the hi/lo tiles (block i covers
 // token rows 4 br.. and channels 16 bc..). All threads call it.
 template <int D, int THREADS, int NB, int LD>
@@ -589,18 +624,12 @@ __device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half
         RgbaOut o;
         uint8_t* codes = &ds.codes[0][tid];
         decode_rgba4(blk, kind, me, cq, codes, NC, o);
-#pragma unroll
-        for (int t = 0; t < 16; ++t) {
-            const int x = t & 3, y = t >> 2;
-            float v[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float s, of;
-                meta_affine(norm, bmoff, bmscl, i, row0 + y, col0 + 4 * x + k, s, of);
-                v[k] = fmaf(c16_to_unit(rgba_c16(o, codes, NC, t, k)), s, of);
-            }
-            put_rgba<LD>(v, y < rows, row0 + y, col0 + 4 * x, thi, tlo);
-        }
+        if (norm == AKV_NORM_PAGE_CHANNEL)
+            write_rgba_n<LD, AKV_NORM_PAGE_CHANNEL>(o, codes, NC, i, bmoff, bmscl, row0, col0, rows, thi, tlo);
+        else if (norm == AKV_NORM_TOKEN)
+            write_rgba_n<LD, AKV_NORM_TOKEN>(o, codes, NC, i, bmoff, bmscl, row0, col0, rows, thi, tlo);
+        else
+            write_rgba_n<LD, AKV_NORM_BLOCK_AFFINE>(o, codes, NC, i, bmoff, bmscl, row0, col0, rows, thi, tlo);
     }
     __syncthreads();
 }

@@ -469,6 +469,8 @@ __device__ __forceinline__ void decode_rgba4(uint4 blk, int kind, uint32_t me, i
     o.cst = kind == kKindConst;
     o.pat = 0u;
     o.wun = T.wunq[mode_wq(me)];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o.e0[c] = o.e1[c] = o.c16[c] = 0u;
     if (o.cst) {
         const uint32_t err[4] = {0xFFFFu, 0u, 0xFFFFu, 0xFFFFu};  // error colour (1, 0, 1, 1)
         // A valid void extent carries RGBA UNORM16 in bits 64..127.
@@ -493,8 +495,6 @@ __device__ __forceinline__ void decode_rgba4(uint4 blk, int kind, uint32_t me, i
         mask_u128(clo, chi, bise_stream_bits_dev(8 * parts, cq));
         color_values(clo, chi, cq, 8 * parts, codes, nt);
     }
-#pragma unroll
-    for (int c = 0; c < 4; ++c) o.e0[c] = o.e1[c] = 0u;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         if (q < parts) {
@@ -522,13 +522,20 @@ __device__ __forceinline__ void decode_rgba4(uint4 blk, int kind, uint32_t me, i
     weight_codes(s0, s1, mode_wq(me), 16, codes, nt);
 }
 
-// UNORM16 value of channel c of texel t of a fast / constant RGBA block.
-__device__ __forceinline__ uint32_t rgba_c16(const RgbaOut& o, const uint8_t* codes, int nt, int t, int c) {
-    if (o.cst) return o.c16[c];
-    const uint32_t part = (o.pat >> (2 * t)) & 3u;
+// The four channels of texel t of a fast / constant RGBA block as 2^16 times
+// their unit values (the fp16 view of C as an integer-valued float, 65535 ->
+// 65536): the weight once per texel, each channel's endpoint bytes of the
+// texel's partition by one byte permute (selector nibbles 4 pick zero bytes).
+__device__ __forceinline__ void rgba_t4(const RgbaOut& o, const uint8_t* codes, int nt, int t, float (&tv)[4]) {
+    const uint32_t sel = ((o.pat >> (2 * t)) & 3u) | 0x4440u;
     const uint32_t w = __ldg(o.wun + codes[t * nt]);
-    const uint32_t X = ((o.e0[c] >> (8 * part)) & 0xFFu) * (64u - w) + ((o.e1[c] >> (8 * part)) & 0xFFu) * w;
-    return 4u * X + ((X + 32u) >> 6);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t e0 = __byte_perm(o.e0[c], 0u, sel), e1 = __byte_perm(o.e1[c], 0u, sel);
+        const uint32_t X = e0 * (64u - w) + e1 * w;
+        const uint32_t c16 = o.cst ? o.c16[c] : 4u * X + ((X + 32u) >> 6);
+        tv[c] = __int_as_float(__float_as_int(static_cast<float>(c16 + (c16 == 0xFFFFu))) & 0xFFFFE000);
+    }
 }
 
 }  // namespace fast

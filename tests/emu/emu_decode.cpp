@@ -220,8 +220,11 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
         std::memset(codes, 0xEE, sizeof(codes));
         F::RgbaOut r;
         F::decode_rgba4(b, kind, me, cq, codes, 1, r);
-        for (int t = 0; t < 16; ++t)
-            for (int k = 0; k < 4; ++k) o[4 * t + k] = akv::c16_to_unit(F::rgba_c16(r, codes, 1, t, k));
+        for (int t = 0; t < 16; ++t) {
+            float tv[4];
+            F::rgba_t4(r, codes, 1, t, tv);
+            for (int k = 0; k < 4; ++k) o[4 * t + k] = tv[k] * 0x1p-16f;
+        }
     }
     return 0;
 }
