@@ -323,7 +323,7 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
             if (x < cols) {
                 const int i = y * BS + x;
                 uint32_t h, l;
-                const uint32_t c0 = codes[i * nt] & o.cmask, c1 = codes[(i + 1) * nt] & o.cmask;
+                const uint32_t c0 = codes[i * nt], c1 = codes[(i + 1) * nt];
                 const uint32_t p0 = (o.pat[i >> 4] >> (2 * (i & 15))) & 3u;
                 const uint32_t p1 = (o.pat[(i + 1) >> 4] >> (2 * ((i + 1) & 15))) & 3u;
                 const uint32_t a = tab[(p0 * L + c0) * nt], b2 = tab[(p1 * L + c1) * nt];

@@ -288,7 +288,11 @@ __device__ __forceinline__ void decode_lum(uint4 blk, int kind, uint32_t me, int
     for (int k = 0; k < 4; ++k) o.pat[k] = 0u;
     if (!lum) {
         if constexpr (kDirect<BS>) o.cu = c16_to_unit(const_c16(blk));
-        else tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+        else {
+            // Every texel reads entry 0: a one-entry table and zero codes.
+            tab[0] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+            for (int t = 0; t < N; ++t) codes[t * nt] = 0;
+        }
         return;
     }
     int v[8];
