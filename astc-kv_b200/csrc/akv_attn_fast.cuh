@@ -237,7 +237,8 @@ __device__ __noinline__ void eval_row_generic(const BlockDesc<1>& d, const uint8
 }
 
 // The 2^16 u values tv of a directly evaluated block, normalised (NORM fixed
-// per instantiation) -> the hi/lo tiles; rows at or past `rows` as zeros.
+// per instantiation) -> the hi/lo tiles (rows past the chunk's tokens are
+// zeroed afterwards by the kernel).
 template <int BS, int LD, int NORM>
 __device__ __forceinline__ void write_direct_n(const float (&tv)[BS * BS], float sc, float of, const __half* moff,
                                                const __half* mscl, int row0, int col0, int rows, __half (*thi)[LD],
@@ -262,7 +263,6 @@ __device__ __forceinline__ void write_direct_n(const float (&tv)[BS * BS], float
             const float s0 = NORM == AKV_NORM_TOKEN ? rs : cs[x], s1 = NORM == AKV_NORM_TOKEN ? rs : cs[x + 1];
             const float o0 = NORM == AKV_NORM_TOKEN ? ro : co[x], o1 = NORM == AKV_NORM_TOKEN ? ro : co[x + 1];
             split_pair(fmaf(tv[y * BS + x], s0, o0), fmaf(tv[y * BS + x + 1], s1, o1), h, l);
-            if (y >= rows) { h = 0u; l = 0u; }
             *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
             *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
         }
@@ -297,7 +297,8 @@ __device__ __forceinline__ void write_direct(const LumOut& o, const uint8_t* cod
 
 // Texels of one table / constant block -> the hi/lo tiles (pairs of columns
 // per 32-bit store), from the value table or, for kDirect footprints, from
-// endpoints and weights. Rows at or past `rows` are written as zeros.
+// endpoints and weights. Rows past the chunk's tokens are written like the
+// others and zeroed afterwards by the kernel.
 template <int BS, int LD>
 __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab, const uint8_t* codes, int nt,
                                             int norm, float sc, float of, const __half* moff, const __half* mscl,
@@ -312,9 +313,8 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
     const uint32_t L = static_cast<uint32_t>(o.L);
 #pragma unroll
     for (int y = 0; y < BS; ++y) {
-        const bool rok = y < rows;
         float rs = 0.f, ro = 0.f;
-        if (norm == AKV_NORM_TOKEN && rok) {
+        if (norm == AKV_NORM_TOKEN) {
             rs = __half2float(mscl[row0 + y]);
             ro = __half2float(moff[row0 + y]);
         }
@@ -338,7 +338,6 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
                     }
                     split_pair(fmaf(__uint_as_float(a), s0, o0), fmaf(__uint_as_float(b2), s1, o1), h, l);
                 }
-                if (!rok) { h = 0u; l = 0u; }
                 *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
                 *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
             }
@@ -873,6 +872,24 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, 3) attn_fast
                 }
                 __syncthreads();
             }
+        }
+        // Rows past the chunk's last token (every row of an unmapped page)
+        // must be zero in the tiles: the table and direct writers store
+        // whatever the staged blocks decode to there. Only a split's last,
+        // partial chunk has such rows.
+        if (n < CH || !valid) {
+            const int r0 = valid ? n : 0;
+            constexpr int Q = LD / 8;  // 16-byte words per tile row
+            for (int i = tid; i < (CH - r0) * Q; i += THREADS) {
+                const int r = r0 + i / Q, k = 8 * (i % Q);
+                *reinterpret_cast<uint4*>(&sm.vhi[r][k]) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(&sm.vlo[r][k]) = make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (KBS > 0) {
+                    *reinterpret_cast<uint4*>(&sm.khi[r][k]) = make_uint4(0u, 0u, 0u, 0u);
+                    *reinterpret_cast<uint4*>(&sm.klo[r][k]) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            __syncthreads();
         }
         // Direct FP16 K fragments for this warp's 16 tokens (loaded after the
         // decode so they do not hold registers through it). Permuted dims:

@@ -63,8 +63,10 @@ def test_golden_kv_page_channel_fixture_positions(cuda):
 
 
 def _cfg_case(B, Hq, Hkv, D, T, *, kfmt, vfmt, seed, page_tokens, q_dtype=torch.float32, lens=None, split=0,
-              paged=False, side=0):
-    """Build a synthetic cache, run the kernel, compare with float64 NumPy."""
+              paged=False, side=0, bad=None):
+    """Build a synthetic cache, run the kernel, compare with float64 NumPy.
+    bad=(b, logical page): that block-table entry points past the pool; the
+    reference then reads that page's K and V as zeros (the kernel's rule)."""
     from astc_kv_cuda.ops import contiguous_fp16_plane, paged_astc_plane, paged_fp16_plane
     rng = np.random.default_rng(seed)
     xk, ch = kv_values(rng, B, Hkv, T, D, outliers=2)
@@ -124,9 +126,19 @@ def _cfg_case(B, Hq, Hkv, D, T, *, kfmt, vfmt, seed, page_tokens, q_dtype=torch.
                 dev[name] = device_astc_plane(p, block=block, layout=layout, normalization=norm,
                                               page_tokens=page_tokens, dim=D)
     lens_t = torch.from_numpy(np.asarray(lens, np.int32)).cuda() if lens is not None else None
+    extra = {}
+    if bad is not None:
+        table = table.copy()
+        table[bad] = num_pages + 5
+        for name in ("k", "v"):
+            restored[name] = restored[name].copy()
+            restored[name][bad[0], :, bad[1] * page_tokens:(bad[1] + 1) * page_tokens] = 0.0
+        extra["status"] = torch.zeros(1, dtype=torch.int32, device="cuda")
     bt = torch.from_numpy(table).cuda() if table is not None else None
     got = run(qt, dev["k"], dev["v"], page_tokens=page_tokens, max_tokens=T, seq_lens=lens_t, block_table=bt,
-              num_pages=num_pages, split_tokens=split)
+              num_pages=num_pages, split_tokens=split, **extra)
+    if bad is not None:
+        assert int(extra["status"].item()) == 5  # AKV_ERR_BAD_BLOCK_TABLE
     ref = O.attention_f64(qn, restored["k"], restored["v"], lens)
     if lens is not None:
         for b, n in enumerate(lens):
@@ -171,6 +183,17 @@ def test_config4_ragged_paged_atlas(cuda):
     got, ref = _cfg_case(4, 32, 8, 128, 1024, kfmt=None, vfmt=(4, "scalar", "block_affine"), seed=4, page_tokens=256,
                          lens=lens, paged=True)
     assert_attention_close(got, ref, "config4")
+
+
+@pytest.mark.parametrize("vfmt", [(4, "scalar", "block_affine"), (6, "scalar", "block_affine")])
+def test_fused_kernel_unmapped_page_reads_zeros(cuda, vfmt):
+    """Fused kernel, paged ASTC V: an out-of-range block-table entry sets the
+    status and that page's tokens read as zero K and V; the sequence's other
+    pages, with a partial last chunk, are unaffected."""
+    P = 96 if vfmt[0] == 6 else 64
+    got, ref = _cfg_case(2, 32, 8, 128, 4 * P, kfmt=None, vfmt=vfmt, seed=17, page_tokens=P,
+                         lens=[4 * P, 2 * P + 29], paged=True, bad=(1, 1))
+    assert_attention_close(got, ref, f"unmapped page {vfmt}")
 
 
 @pytest.mark.parametrize("T,split,lens", [(384, 6, None), (96, 12, [1]), (96, 48, [7]), (480, 24, [391]),
