@@ -158,7 +158,7 @@ __device__ __noinline__ void eval_block_generic(uint4 blk, int norm, float sc, f
                                                 const __half* mscl, int row0, int col0, int rows, int ncol,
                                                 __half (*thi)[LD], __half (*tlo)[LD]) {
     BlockDesc<1> d;
-    uint8_t wl[64];
+    uint8_t wl[64 + kCodePad];
     decode_header<1>(blk, footprint_index(BS), d, wl);
     for (int t = 0; t < BS * BS; ++t) {
         const int x = t % BS, y = t / BS;
@@ -542,7 +542,7 @@ template <int LD>
 __device__ __noinline__ void eval_rgba_generic(uint4 blk, int i, int norm, const __half* moff, const __half* mscl,
                                                int row0, int col0, int rows, __half (*thi)[LD], __half (*tlo)[LD]) {
     BlockDesc<4> d;
-    uint8_t w[64];
+    uint8_t w[64 + kCodePad];
     decode_header<4>(blk, footprint_index(4), d, w);
     for (int t = 0; t < 16; ++t) {
         const int x = t & 3, y = t >> 2;

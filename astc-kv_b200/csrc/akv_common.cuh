@@ -77,7 +77,7 @@ template <int BS, int LAYOUT>
 struct TileScratch {
     static constexpr int NCH = LAYOUT == AKV_LAYOUT_RGBA ? 4 : 1;
     BlockDesc<NCH> desc[kMaxBlocks];
-    uint8_t wts[kMaxBlocks][64];
+    uint8_t wts[kMaxBlocks][64 + kCodePad];
     float2 aff[kMaxBlocks];
 };
 

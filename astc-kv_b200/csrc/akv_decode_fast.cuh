@@ -94,61 +94,6 @@ __device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
     return kKindTable;
 }
 
-// BISE weight codes: `count` values of range wq from the bit-reversed weight
-// stream (s0, s1), already masked to its length, into codes[i * nt]. Groups
-// of five (trits, plain bits) or three (quints) values per step, with the
-// trit/quint block bits gathered by runtime shifts and decoded through the
-// combined digit table. Every step stores five codes without predicates: a
-// quint step's two extra codes are overwritten by the next step, and the
-// last step may write up to four rows past `count` (the caller provides
-// kCodePad rows of slack).
-constexpr int kCodePad = 4;
-
-__device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, int count, uint8_t* codes, int nt) {
-    const Tables& T = g_akv_tables;
-    const uint32_t shp = __ldg(&T.shape[wq]);
-    const int b = shp & 15;
-    const bool tr = (shp >> 4) & 1, qu = (shp >> 5) & 1;
-    const int gs = qu ? 3 : 5;
-    const int gb = tr ? 5 * b + 8 : (qu ? 3 * b + 7 : 5 * b);
-    const int ng = qu ? (count + 2) / 3 : (count + 4) / 5;
-    // Masks of the trit / quint block bits after shifting by k * b.
-    const uint32_t m1 = tr ? 0x03u : (qu ? 0x07u : 0u);
-    const uint32_t m2 = tr ? 0x0Cu : (qu ? 0x18u : 0u);
-    const uint32_t m3 = tr ? 0x10u : (qu ? 0x60u : 0u);
-    const uint32_t m4 = tr ? 0x60u : 0u;
-    const uint32_t m5 = tr ? 0x80u : 0u;
-    // Offsets of the low bits of values 1..4 within a group.
-    const int o1 = b + (tr ? 2 : (qu ? 3 : 0));
-    const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
-    const int o3 = 3 * b + (tr ? 5 : 0);
-    const int o4 = 4 * b + (tr ? 7 : 0);
-    const int b2 = 2 * b, b3 = 3 * b, b4 = 4 * b, b5 = 5 * b;
-    const uint16_t* dig = T.dig3 + (qu ? 256 : 0);
-    const uint32_t bm = (1u << b) - 1u, km = 7u << b;
-    // The stream as four 32-bit words, shifted down by `gb` per step.
-    uint32_t w0 = static_cast<uint32_t>(s0), w1 = static_cast<uint32_t>(s0 >> 32);
-    uint32_t w2 = static_cast<uint32_t>(s1), w3 = static_cast<uint32_t>(s1 >> 32);
-    uint8_t* cp = codes;
-    const int step = gs * nt;
-    for (int g = 0; g < ng; ++g) {
-        const uint32_t win = w0;
-        const uint32_t X = ((win >> b) & m1) | ((win >> b2) & m2) | ((win >> b3) & m3) | ((win >> b4) & m4) |
-                           ((win >> b5) & m5);
-        const uint32_t dgb = static_cast<uint32_t>(__ldg(dig + X)) << b;
-        cp[0] = static_cast<uint8_t>((dgb & km) | (win & bm));
-        cp[nt] = static_cast<uint8_t>(((dgb >> 3) & km) | ((win >> o1) & bm));
-        cp[2 * nt] = static_cast<uint8_t>(((dgb >> 6) & km) | ((win >> o2) & bm));
-        cp[3 * nt] = static_cast<uint8_t>(((dgb >> 9) & km) | ((win >> o3) & bm));
-        cp[4 * nt] = static_cast<uint8_t>(((dgb >> 12) & km) | ((win >> o4) & bm));
-        cp += step;
-        w0 = __funnelshift_r(w0, w1, gb);
-        w1 = __funnelshift_r(w1, w2, gb);
-        w2 = __funnelshift_r(w2, w3, gb);
-        w3 >>= gb;
-    }
-}
-
 // The first nv (<= 8) colour integers of range cq from the colour stream
 // (s0, s1), masked to its length, unquantised to 0..255 into out[j * nt]:
 // one runtime step loop for trit, quint and plain-bit ranges alike (64-bit

@@ -21,7 +21,7 @@ template <int BS, int MODE, bool VEC>
 __global__ void __launch_bounds__(kDecodeThreads, 3) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
                                                                           void* __restrict__ out) {
     __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
-    __shared__ uint8_t wts[kDecodeBlocksPerIter][68];
+    __shared__ uint8_t wts[kDecodeBlocksPerIter][64 + kCodePad];
     constexpr int fp = footprint_index(BS);
     constexpr int TPB = BS * BS;
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * kDecodeBlocksPerIter; base < n;
@@ -73,7 +73,7 @@ template <int BS>
 __global__ void __launch_bounds__(kDecodeThreads) decode_image_kernel(const uint4* __restrict__ blocks, int cols, int rows,
                                                                       float* __restrict__ rgba, int w, int h) {
     __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
-    __shared__ uint8_t wts[kDecodeBlocksPerIter][64];
+    __shared__ uint8_t wts[kDecodeBlocksPerIter][64 + kCodePad];
     constexpr int fp = footprint_index(BS);
     constexpr int TPB = BS * BS;
     const int64_t n = static_cast<int64_t>(cols) * rows;

@@ -53,7 +53,7 @@ extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, u
         uint4 b;
         std::memcpy(&b, blocks + 16 * i, 16);
         akv::BlockDesc<4> d;
-        uint8_t w[64];
+        uint8_t w[64 + akv::kCodePad];
         std::memset(w, 0, sizeof(w));
         akv::decode_header<4>(b, fp, d, w);
         for (int y = 0; y < bs; ++y)
@@ -91,7 +91,7 @@ extern "C" int emu_decode_rows_u16(const uint8_t* blocks, int64_t n, int bs, uin
         uint4 b;
         std::memcpy(&b, blocks + 16 * i, 16);
         akv::BlockDesc<4> d;
-        uint8_t w[64];
+        uint8_t w[64 + akv::kCodePad];
         std::memset(w, 0xEE, sizeof(w));  // unwritten weights must not matter
         akv::decode_header<4>(b, fp, d, w);
         uint16_t* o = out + i * bs * bs * 4;
@@ -142,7 +142,7 @@ static int fast_r_one(uint4 b, int* kind_out, float* out) {
         return 0;
     }
     uint32_t tab[F::kTabCapMax];
-    uint8_t codes[64 + akv::fast::kCodePad];
+    uint8_t codes[64 + akv::kCodePad];
     std::memset(codes, 0xEE, sizeof(codes));  // stale bytes must not matter for constant blocks
     akv::BlockDesc<1> d;
     alignas(16) uint8_t w[72];
@@ -207,7 +207,7 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
         float* o = out + i * 64;
         if (kind == F::kKindGeneric) {
             akv::BlockDesc<4> d;
-            uint8_t w[64];
+            uint8_t w[64 + akv::kCodePad];
             akv::decode_header<4>(b, akv::footprint_index(4), d, w);
             for (int t = 0; t < 16; ++t) {
                 uint32_t c[4];
@@ -216,7 +216,7 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
             }
             continue;
         }
-        uint8_t codes[16 + F::kCodePad];
+        uint8_t codes[16 + akv::kCodePad];
         std::memset(codes, 0xEE, sizeof(codes));
         F::RgbaOut r;
         F::decode_rgba4(b, kind, me, cq, codes, 1, r);
