@@ -320,7 +320,11 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
         }
 #pragma unroll
         for (int x = 0; x < BS; x += 2) {
-            if (x < cols) {
+            // No column check: a block overhanging the head dimension (6x6)
+            // writes its extra columns into the tile rows' padding (LD =
+            // D + 8) and reads metadata inside the chunk's metadata array;
+            // neither is read for results.
+            {
                 const int i = y * BS + x;
                 uint32_t h, l;
                 const uint32_t c0 = codes[i * nt], c1 = codes[(i + 1) * nt];
@@ -662,6 +666,9 @@ struct Cfg {
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
+    // Overhanging block columns stay inside the tile rows and metadata.
+    static_assert((D + VBS - 1) / VBS * VBS <= LD && (!KBS || (D + KBS - 1) / KBS * KBS <= LD), "tile row padding");
+    static_assert(VL == AKV_LAYOUT_RGBA || (D + VBS - 1) / VBS * VBS <= META, "metadata padding");
     static_assert(VL == AKV_LAYOUT_SCALAR || (VBS == 4 && KBS == 0 && D % 16 == 0), "RGBA: 4x4 V, FP16 K");
 };
 
@@ -687,8 +694,13 @@ struct Smem {
     float wl[C::NWM][8];
 };
 
+// Three CTAs per SM, except scalar 4x4 V with FP16 K (256 threads): two CTAs
+// with up to 128 registers instead of spilling at 80 (C4 9.7 ms against 10.5;
+// the RGBA 4x4 instances are faster with three).
 template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
-__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, 3) attn_fast_kernel(AttnParams p) {
+__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
+                                  (VBS == 4 && KBS == 0 && VL == AKV_LAYOUT_SCALAR) ? 2 : 3)
+    attn_fast_kernel(AttnParams p) {
     using C = Cfg<D, G, VBS, KBS, VL>;
     using S = Smem<D, G, VBS, KBS, VL>;
     constexpr int CH = C::CH, NWM = C::NWM, THREADS = C::THREADS, LD = C::LD;
