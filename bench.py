@@ -255,7 +255,7 @@ def run_decode(args) -> dict | None:
 class Workload:
     """Device-resident inputs of one rank plus the prepared attention call."""
 
-    def __init__(self, name: str, rank: int, device, batch: int = 0):
+    def __init__(self, name: str, rank: int, device, batch: int = 0, split_tokens: int = 0):
         import torch
         from astc_kv_cuda.ops import (Attention, contiguous_astc_plane, contiguous_fp16_plane, paged_astc_plane,
                                       paged_fp16_plane)
@@ -376,6 +376,8 @@ class Workload:
             raise SystemExit(f"unknown workload {name}")
         self.q = q
         self.tokens = int(sum(self.lens))
+        if split_tokens:
+            split = split_tokens  # explicit split (profiling a small case with the full run's splits)
         self.attn = Attention(q, self.kp, self.vp, page_tokens=P, max_tokens=T, seq_lens=self.seq_lens,
                               block_table=self.table, num_pages=num_pages, split_tokens=split)
         self.B = B
@@ -394,7 +396,7 @@ def run_ours(args) -> dict | None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     import astc_kv_cuda as A
     A.init(local)
-    wl = Workload(args.workload, rank, dev, args.batch)
+    wl = Workload(args.workload, rank, dev, args.batch, args.split_tokens)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -593,6 +595,9 @@ def main():
     ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4", "decode4", "decode6", "decode8"], default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--batch", type=int, default=0, help="override the per-GPU batch (profiling of small cases)")
+    ap.add_argument("--split-tokens", type=int, default=0,
+                    help="tokens per split (0: the library's automatic choice; set it to profile a small batch "
+                         "with the full run's split structure)")
     ap.add_argument("--decode-blocks", type=int, default=1 << 26,
                     help="blocks per step of the decode microbench (a multiple of 2^20; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
