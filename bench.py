@@ -478,10 +478,10 @@ def run_ours(args) -> dict | None:
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of
 # the split kernel from the committed ncu captures (profiles/), bytes: c2 was
-# captured at batch 4 (353.3 MB) and scaled by the 8x units of the batch-32
+# captured at batch 4 with the full run's splits (353.1 MB) and scaled by the 8x units of the batch-32
 # launch, c3 at batch 1 (220.3 MB) and scaled by the 8x units of the batch-8
 # launch (traffic grows with the batch).
-TRAFFIC: dict[str, float | None] = {"c2": 353.297e6 * 8, "c3": 220.313e6 * 8}
+TRAFFIC: dict[str, float | None] = {"c2": 353.055e6 * 8, "c3": 220.313e6 * 8}
 
 
 # ------------------------------------------------------------- CPU reference path
