@@ -71,3 +71,75 @@ def load_manifest(directory: str | Path) -> dict:
             entry["decoded"] = np.fromfile(root / m[side + "_decoded_file"], "<f4").reshape(Hkv, T, D)
         out[side] = entry
     return out
+
+
+def write_manifest(directory: str | Path, q: np.ndarray, k, v, *, page_tokens: int, layout: str = "scalar",
+                   tokens: int | None = None, extra: dict | None = None, with_decoded: bool = True) -> dict:
+    """Write an astc-kv-probe-v1 fixture (the reader above loads it back).
+
+    `q` is float32 [Hq, D]; `k` / `v` are each either an ``EncodedTensor``
+    (written as one ``.astc`` file per head plus fp16 offsets / scales and the
+    fp32 restore) or a float array [Hkv, T, D] (written as FP16). Field names,
+    file naming and byte accounting follow the reference's exporter
+    (scripts/export_metal_fixture.py:31-63, docs/metal_path.md:50-73):
+    ``logical_cache_bytes`` per ASTC side equals the tensor's ``byte_counts``
+    (blocks with edge padding, fp16 offsets, fp16 scales). Token-normalised
+    metadata is cut to the real tokens. ``with_decoded=False`` leaves out the
+    optional ``*_decoded.f32`` restores (an ASTC side's restore runs on the
+    GPU). Returns the manifest.
+    """
+    from .codec import EncodedTensor
+    root = Path(directory)
+    root.mkdir(parents=True, exist_ok=True)
+    q = np.asarray(q, np.float32)
+    hq, dim = q.shape
+    sides = {"k": k, "v": v}
+    kvh = {s: (x.heads if isinstance(x, EncodedTensor) else np.asarray(x).shape[0]) for s, x in sides.items()}
+    if kvh["k"] != kvh["v"]:
+        raise ValueError("K and V must have the same kv heads")
+    t_all = {s: (x.tokens if isinstance(x, EncodedTensor) else np.asarray(x).shape[1]) for s, x in sides.items()}
+    t = tokens if tokens is not None else min(t_all.values())
+    if all(not isinstance(x, EncodedTensor) for x in sides.values()):
+        raise ValueError("At least one side must use ASTC for this probe")
+    q.astype("<f4").tofile(root / "q.f32")
+    m = {"format": "astc-kv-probe-v1", "tokens": int(t), "query_heads": int(hq), "kv_heads": int(kvh["k"]),
+         "head_dim": int(dim), "page_tokens": int(page_tokens), "layout": layout, "metadata_dtype": "float16_le",
+         "query_file": "q.f32", "logical_cache_bytes": {}, "file_header_bytes": 0, **(extra or {})}
+    for name, x in sides.items():
+        if isinstance(x, EncodedTensor):
+            m[name + "_storage"] = "astc"
+            files = []
+            for h in range(x.heads):
+                fn = f"{name}-h{h:03d}.astc"
+                (root / fn).write_bytes(x.astc_file(h))
+                files.append(fn)
+            m[name + "_files"] = files
+            m[name + "_normalization"] = x.normalization
+            off, scl = x.offsets, x.scales
+            if x.normalization == "token":
+                off, scl = off[:, :t], scl[:, :t]
+            for suffix, a in (("offset", off), ("scale", scl)):
+                fn = f"{name}_{suffix}.f16"
+                np.asarray(a, "<f2").tofile(root / fn)
+                m[f"{name}_{suffix}_file"] = fn
+            decoded = np.asarray(x.decoded, np.float32)[:, :t] if with_decoded else None
+            m["logical_cache_bytes"][name] = {"astc_blocks_with_padding": int(sum(map(len, x.payloads))),
+                                              "fp16_offsets": int(np.asarray(off).nbytes),
+                                              "fp16_scales": int(np.asarray(scl).nbytes)}
+            m["file_header_bytes"] += 16 * x.heads
+        else:
+            xa = np.asarray(x, np.float32)[:, :t]
+            fn = name + ".f16"
+            xa.astype("<f2").tofile(root / fn)
+            m[name + "_storage"] = "fp16"
+            m[name + "_file"] = fn
+            decoded = xa.astype(np.float16).astype(np.float32)
+            m["logical_cache_bytes"][name] = {"fp16_payload": int(xa.size * 2)}
+        if with_decoded:
+            fn = name + "_decoded.f32"
+            decoded.astype("<f4").tofile(root / fn)
+            m[name + "_decoded_file"] = fn
+    scalars = 2 * kvh["k"] * t * dim
+    m["logical_bits_per_original_kv_scalar"] = sum(sum(b.values()) for b in m["logical_cache_bytes"].values()) * 8 / scalars
+    (root / "manifest.json").write_text(json.dumps(m, indent=2) + "\n")
+    return m

@@ -839,7 +839,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
 #pragma unroll
     for (int i = 0; i < KH; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F}, l_run[2] = {0.f, 0.f};
-    bool stuck = false;
+    int stuck = -1;  // chunk whose copies did not arrive in time
 
     for (int c = 0; c < nchunks; ++c) {
         const int s = c & 1;
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         const int n = min(CH, t_end - t0);
         const bool waited = mbar_wait(&sm.bar[s], parity);
         if (__syncthreads_or(!waited)) {
-            stuck = true;
+            stuck = c;
             break;
         }
         const bool valid = sm.valid[s] != 0;
@@ -1027,13 +1027,17 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         __syncthreads();  // tiles and P buffers free for the next chunk
     }
 
-    if (stuck) {
-        // A copy never completed: report, give in-flight copies a bounded
-        // grace period, and leave this split empty.
+    if (stuck >= 0) {
+        // A copy never completed: report, give the copies still in flight
+        // (chunk `stuck` and, if it was issued, chunk stuck + 1, one per
+        // stage) a bounded grace period each so none lands in shared memory
+        // after the CTA exits, and leave this split empty.
         if (tid == 0) {
             if (p.status) atomicExch(p.status, AKV_ERR_TIMEOUT);
-            mbar_wait(&sm.bar[0], 0);
+            mbar_wait(&sm.bar[stuck & 1], (stuck >> 1) & 1);
+            if (stuck + 1 < nchunks) mbar_wait(&sm.bar[(stuck + 1) & 1], ((stuck + 1) >> 1) & 1);
         }
+        __syncthreads();
         for (int i = tid; i < G * D; i += THREADS)
             p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = 0.f;
         if (tid < G) {

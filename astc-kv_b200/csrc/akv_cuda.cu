@@ -5,6 +5,7 @@
 // akv_decode_kernels.cuh and akv_attention_kernels.cuh.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -26,7 +27,10 @@ static __device__ __align__(256) float g_static_workspace[AKV_STATIC_WORKSPACE_B
 
 constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
-bool g_init_done[kMaxDevices];
+// Per-device "tables uploaded" flags. They live as long as the process: after
+// a cudaDeviceReset the device's static memory is gone but the flag is not,
+// so a caller that resets a device must not use this library on it again.
+std::atomic<bool> g_init_done[kMaxDevices];
 Tables* g_host_tables = nullptr;
 
 const Tables& host_tables() {
@@ -41,7 +45,7 @@ const Tables& host_tables() {
 int init_device(int device) {
     if (device < 0 || device >= kMaxDevices) return AKV_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> lock(g_init_mu);
-    if (g_init_done[device]) return AKV_OK;
+    if (g_init_done[device].load(std::memory_order_acquire)) return AKV_OK;
     int prev = -1;
     if (cudaGetDevice(&prev) != cudaSuccess) return AKV_ERR_CUDA;
     if (prev != device && cudaSetDevice(device) != cudaSuccess) return AKV_ERR_CUDA;
@@ -50,18 +54,36 @@ int init_device(int device) {
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (prev != device) cudaSetDevice(prev);
     if (e != cudaSuccess) return AKV_ERR_CUDA;
-    g_init_done[device] = true;
+    g_init_done[device].store(true, std::memory_order_release);
     return AKV_OK;
 }
 
-int ensure_init() {
+// True when `s` (or, in global capture mode elsewhere, the legacy stream) is
+// being captured; a failing query counts as capturing.
+bool capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) {
+        cudaGetLastError();
+        return true;
+    }
+    if (cap != cudaStreamCaptureStatusNone) return true;
+    if (s != nullptr && s != cudaStreamLegacy) {
+        if (cudaStreamIsCapturing(cudaStreamLegacy, &cap) != cudaSuccess) {
+            cudaGetLastError();
+            return true;
+        }
+        return cap != cudaStreamCaptureStatusNone;
+    }
+    return false;
+}
+
+// Tables of the current device, uploaded on first use. The upload is
+// synchronous, so it is refused while the call's stream is being captured.
+int ensure_init(cudaStream_t stream) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return AKV_ERR_CUDA;
-    if (dev >= 0 && dev < kMaxDevices && g_init_done[dev]) return AKV_OK;
-    // Table upload is synchronous; refuse inside a stream capture.
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(cudaStreamLegacy, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
-        return AKV_ERR_NOT_INITIALIZED;
+    if (dev >= 0 && dev < kMaxDevices && g_init_done[dev].load(std::memory_order_acquire)) return AKV_OK;
+    if (capturing(stream)) return AKV_ERR_NOT_INITIALIZED;
     return init_device(dev);
 }
 
@@ -209,8 +231,10 @@ bool fast_path_ok(const AkvAttnDesc* d, int kbs, int vbs, int vl, int split) {
     if (P % CH) {
         // Several pages per chunk: RGBA V of a contiguous cache only, pages of
         // at least 16 tokens, consecutive pages adjacent in memory (one copy
-        // per chunk) with their metadata.
-        if (vl != AKV_LAYOUT_RGBA || d->block_table_dev || CH % P || P < 16) return false;
+        // per chunk) with their metadata. Every chunk copies CH / P whole
+        // pages, so the capacity (max_tokens) must be whole chunks: the last
+        // chunk's copy then ends inside the plane.
+        if (vl != AKV_LAYOUT_RGBA || d->block_table_dev || CH % P || P < 16 || d->max_tokens % CH) return false;
         const AkvPlane& v = d->v;
         const int cols = d->head_dim / (4 * v.block);
         const int64_t per_page = v.normalization == AKV_NORM_BLOCK_AFFINE ? (P / v.block) * cols
@@ -274,7 +298,10 @@ struct AttnPlan {
     size_t ws;
 };
 
-int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
+// `ws_limit` > 0: when the caller leaves the split to the library and the
+// default split's partials need more than ws_limit bytes, the plan takes the
+// most splits whose partials fit instead (fewer, longer splits).
+int plan_attention(const AkvAttnDesc* d, AttnPlan* out, size_t ws_limit = 0) {
     if (!d) return AKV_ERR_INVALID_ARGUMENT;
     if (d->batch <= 0 || d->q_heads <= 0 || d->kv_heads <= 0 || d->head_dim <= 0 || d->max_tokens <= 0 ||
         d->page_tokens <= 0 || d->q_heads % d->kv_heads)
@@ -329,6 +356,22 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out) {
         int a = lcm_fp, b = out->vbs;
         while (b) { const int r = a % b; a = b; b = r; }
         lcm_fp = lcm_fp / a * out->vbs;
+    }
+    const size_t per_split = static_cast<size_t>(d->batch) * d->q_heads * (d->head_dim + 2) * sizeof(float);
+    if (d->split_tokens <= 0 && ws_limit > 0 &&
+        per_split * static_cast<size_t>((d->max_tokens + split - 1) / split) > ws_limit) {
+        const int64_t nmax = static_cast<int64_t>(ws_limit / per_split);
+        if (nmax < 1) return AKV_ERR_STATIC_WORKSPACE;
+        // Splits stay whole chunks and whole block rows of every plane.
+        int align = ch, b = lcm_fp;
+        {
+            int a = align;
+            while (b) { const int r = a % b; a = b; b = r; }
+            align = align / a * lcm_fp;
+        }
+        int64_t per = (d->max_tokens + nmax - 1) / nmax;
+        per = ((per + align - 1) / align) * align;
+        split = static_cast<int>(per);
     }
     if (split % lcm_fp) return AKV_ERR_INVALID_ARGUMENT;
     out->split = split;
@@ -455,7 +498,7 @@ int akv_cuda_decode_blocks(const void* blocks_dev, int64_t nblocks, int block, i
     if (!blocks_dev || !out_dev || reinterpret_cast<uintptr_t>(blocks_dev) % 16 ||
         reinterpret_cast<uintptr_t>(out_dev) % (out_mode == AKV_OUT_UNORM8 ? 4 : 8))
         return AKV_ERR_INVALID_ARGUMENT;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (block) {
         case 4: return launch_decode<4>(blocks_dev, nblocks, out_mode, out_dev, s);
@@ -472,7 +515,7 @@ int akv_cuda_decode_image(const void* blocks_dev, size_t bytes, int block, float
     if (static_cast<size_t>(cols) * rows * 16 != bytes) return AKV_ERR_INVALID_ARGUMENT;
     if (!blocks_dev || !rgba_dev || reinterpret_cast<uintptr_t>(blocks_dev) % 16 || reinterpret_cast<uintptr_t>(rgba_dev) % 16)
         return AKV_ERR_INVALID_ARGUMENT;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t n = static_cast<int64_t>(cols) * rows;
     const int64_t iters = (n + kDecodeBlocksPerIter - 1) / kDecodeBlocksPerIter;
@@ -512,7 +555,7 @@ int akv_cuda_decode_attention_phase(const AkvAttnDesc* d, int phase, void* strea
     if (!d->q_dev || !d->out_dev) return AKV_ERR_INVALID_ARGUMENT;
     if (!d->workspace_dev || d->workspace_bytes < plan.ws) return AKV_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(d->workspace_dev) % 16) return AKV_ERR_INVALID_ARGUMENT;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     const AttnParams p = segment_params(d, plan, d, 0, plan.nsplits);
     return launch_segment(d, plan, p, static_cast<cudaStream_t>(stream), phase);
 }
@@ -531,7 +574,7 @@ int akv_cuda_decode_attention_tail(const AkvAttnDesc* d, const AkvAttnDesc* tail
     if (!d->q_dev || !d->out_dev) return AKV_ERR_INVALID_ARGUMENT;
     if (!d->workspace_dev || d->workspace_bytes < a.ws + b.ws) return AKV_ERR_WORKSPACE;
     if (reinterpret_cast<uintptr_t>(d->workspace_dev) % 16) return AKV_ERR_INVALID_ARGUMENT;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int stride = a.nsplits + b.nsplits;
     AttnParams pa = segment_params(d, a, d, 0, stride);
@@ -546,12 +589,13 @@ int akv_cuda_decode_attention_tail(const AkvAttnDesc* d, const AkvAttnDesc* tail
 
 int akv_cuda_decode_attention_noalloc(const AkvAttnDesc* d, void* stream) {
     AttnPlan plan;
-    if (int st = plan_attention(d, &plan)) return st;
+    if (int st = plan_attention(d, &plan, static_cast<size_t>(AKV_STATIC_WORKSPACE_BYTES))) return st;
     if (plan.ws > static_cast<size_t>(AKV_STATIC_WORKSPACE_BYTES)) return AKV_ERR_STATIC_WORKSPACE;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     void* ws = nullptr;
     if (int st = static_workspace(&ws)) return st;
     AkvAttnDesc local = *d;
+    local.split_tokens = plan.split;  // the split chosen to fit the static array
     local.workspace_dev = ws;
     local.workspace_bytes = AKV_STATIC_WORKSPACE_BYTES;
     return akv_cuda_decode_attention(&local, stream);
@@ -566,7 +610,7 @@ int akv_cuda_restore_plane(const AkvPlane* plane, int32_t batch, int32_t kv_head
     if (block_table_dev && (pages_per_seq <= 0 || num_pages <= 0 ||
                             static_cast<int64_t>(pages_per_seq) * page_tokens < max_tokens))
         return AKV_ERR_INVALID_ARGUMENT;
-    if (int st = ensure_init()) return st;
+    if (int st = ensure_init(static_cast<cudaStream_t>(stream))) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const PlaneDev pl = to_dev(*plane);
     if (plane->storage == AKV_STORAGE_FP16) {

@@ -59,7 +59,11 @@ int akv_cuda_abi_version(void);
 
 /* Fills the decode tables of `device` (synchronous, once per device; later
  * calls return at once). Every other entry point calls it for the current
- * device on first use, so call it yourself before any stream capture. */
+ * device on first use (and returns AKV_ERR_NOT_INITIALIZED instead while the
+ * call's stream is being captured), so call it yourself before any stream
+ * capture. The per-device state lives until the process exits: a device
+ * reset (cudaDeviceReset) drops the tables but not the library's record of
+ * them, so do not use the library on a device after resetting it. */
 int akv_cuda_init(int device);
 
 /*
@@ -202,8 +206,12 @@ int akv_cuda_decode_attention_phase(const AkvAttnDesc* desc, int phase, void* st
  * AKV_STATIC_WORKSPACE_BYTES compiled into the library (every GPU that loads
  * the library holds that array until the process exits). It allocates
  * nothing.
- *   - A descriptor that needs more scratch than that (see
- *     akv_cuda_attention_workspace) returns AKV_ERR_STATIC_WORKSPACE.
+ *   - With split_tokens = 0 the library picks the split: its usual choice
+ *     when those partials fit the array, else the most splits whose
+ *     partials fit (longer splits). A descriptor whose explicit
+ *     split_tokens needs more scratch than the array holds (see
+ *     akv_cuda_attention_workspace), or that does not fit even with one
+ *     split per sequence, returns AKV_ERR_STATIC_WORKSPACE.
  *   - The first call on a device looks up the array's device address (and
  *     fills the decode tables if akv_cuda_init has not run there); make that
  *     first call, or akv_cuda_init plus one call, before any stream capture.

@@ -10,12 +10,14 @@ committed .npz files. Sources, all encoded by Arm astcenc 5.7.0 at quality 98,
 * results/metal_fixtures/story_l17_kv_page6 — K and V ASTC (page_channel).
 * results/block_geometry_v2/<capture>_l<layer>/identity.bin + identity.npy +
   fixed_input.npz — 24 capture/layer pairs (token normalisation, 288 tokens).
+* metrics_golden.npz — the reference's `errors` / `attention_metrics`
+  (codec.py:270-283) evaluated on seeded inputs.
 
 Attention goldens come from importing the reference's own
 astc_kv/codec.py `attention` (codec.py:253-267) on the reference restores.
 Large restores are stored as SHA-256 digests of their float32 bytes.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/reference]
+Usage: python tests/golden/make_golden.py --reference /path/to/reference
 """
 from __future__ import annotations
 
@@ -43,13 +45,42 @@ def read_astc(path: Path) -> tuple[int, int, int, np.ndarray]:
     return b, w, h, np.frombuffer(raw[16:], np.uint8).reshape(h // b, (w + b - 1) // b, 16)
 
 
+def metrics_golden(ref: Path) -> None:
+    """The reference's own `errors` / `attention_metrics` (codec.py:270-283) on
+    seeded inputs: one attention output pair and one probability pair, with
+    the values the reference returns."""
+    from astc_kv.codec import attention_metrics, errors
+    rng = np.random.default_rng(20261030)
+    a = rng.standard_normal((9, 3, 64)).astype(np.float32)
+    b = (a + rng.standard_normal(a.shape) * 1e-3).astype(np.float32)
+    s1 = rng.standard_normal((9, 3, 384))
+    s2 = s1 + rng.standard_normal(s1.shape) * 0.05
+    pa = np.exp(s1 - s1.max(-1, keepdims=True))
+    pa = (pa / pa.sum(-1, keepdims=True)).astype(np.float32)
+    pb = np.exp(s2 - s2.max(-1, keepdims=True))
+    pb = (pb / pb.sum(-1, keepdims=True)).astype(np.float32)
+    e = errors(a, b)
+    m = attention_metrics(a, b, pa, pb)
+    keys_e, keys_m = sorted(e), sorted(m)
+    np.savez_compressed(HERE / "metrics_golden.npz", a=a, b=b, pa=pa, pb=pb,
+                        errors_keys=np.array(keys_e), errors_values=np.array([e[k] for k in keys_e]),
+                        metrics_keys=np.array(keys_m), metrics_values=np.array([m[k] for k in keys_m]))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="checkout of the reference project (BoyJayy/ASTC-KV)")
+    ap.add_argument("--only", choices=["all", "metrics"], default="all",
+                    help="metrics: write only metrics_golden.npz (the other fixtures stay as they are)")
     args = ap.parse_args()
     ref = args.reference
     sys.path.insert(0, str(ref))
     from astc_kv.codec import attention  # the reference implementation
+
+    metrics_golden(ref)
+    if args.only == "metrics":
+        return
 
     # 1. V-only token fixture.
     d = ref / "results/metal_fixtures/story_l17_v_token6"

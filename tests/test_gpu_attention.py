@@ -280,3 +280,22 @@ def test_fused_kernel_on_every_block_mode(cuda, block, D, G, layout, P, norm):
     got = attn.run().cpu().numpy()
     ref = O.attention_f64(q, k.astype(np.float32), vr, lens)
     assert_attention_close(got, ref, f"every-mode {layout} {block}x{block} {norm} D{D} P{P}")
+
+
+def test_rgba_pages_smaller_than_a_chunk_with_a_partial_last_chunk(cuda):
+    """RGBA 4x4 V with 16-token pages puts several pages in one fused-kernel
+    chunk, which copies whole chunks of pages. A capacity of 400 tokens (25
+    pages) is not whole 64-token chunks, so the library must not take that
+    path (its last chunk would copy past the plane); the result must still
+    match the oracle. 384 tokens (whole chunks) keeps the fused kernel."""
+    from astc_kv_cuda.ops import Attention, contiguous_astc_plane, contiguous_fp16_plane
+    got, ref = _cfg_case(1, 9, 3, 64, 400, kfmt=None, vfmt=(4, "rgba", "page_channel"), seed=400, page_tokens=16)
+    assert_attention_close(got, ref, "rgba T=400 P=16")
+    for T, kernel in ((400, "attn_split_kernel"), (384, "attn_fast_kernel")):
+        blocks = torch.zeros(1, 3, T // 4, 4, 16, dtype=torch.uint8, device="cuda")
+        meta = torch.zeros(1, 3, T // 16, 64, dtype=torch.float16, device="cuda")
+        vp = contiguous_astc_plane(blocks, meta, meta, block=4, layout="rgba", normalization="page_channel",
+                                   head_dim=64, page_tokens=16)
+        kp = contiguous_fp16_plane(torch.zeros(1, 3, T, 64, dtype=torch.float16, device="cuda"), 16)
+        q = torch.zeros(1, 9, 64, device="cuda")
+        assert Attention(q, kp, vp, page_tokens=16, max_tokens=T).plan()["kernel"] == kernel, T

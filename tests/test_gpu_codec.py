@@ -74,3 +74,32 @@ def test_codec_attention_mirror_fresh_tail(cuda):
     vall = np.concatenate([ev.decoded, vt16.astype(np.float32)], axis=1)
     ref, _ = O.attention(q, kall, vall, pos)
     assert_attention_close(got, ref, "codec.attention mirror with FP16 tail")
+
+
+def test_probe_fixture_through_the_gpu_attention(cuda, tmp_path):
+    """A fixture written in the reference's astc-kv-probe-v1 format (the
+    reference's own story_l17_v_token6 data), read back by load_manifest and
+    attended on the GPU, reproduces the reference's codec.attention output."""
+    import torch
+    from astc_kv_cuda import interchange as I
+    from astc_kv_cuda.codec import EncodedTensor
+    from astc_kv_cuda.ops import Attention, contiguous_astc_plane, contiguous_fp16_plane
+    from common import assert_attention_close, golden
+    g = golden("story_l17_v_token6")
+    H, T, D = g["k"].shape
+    enc = EncodedTensor(g["v_decoded"], [g["v_blocks"][h].tobytes() for h in range(H)], 66, 384, 6, "scalar", "ldr",
+                        "token", g["v_offset"], g["v_scale"], 96, {}, 0.0, metadata={"dim": D})
+    I.write_manifest(tmp_path, g["q"], g["k"].astype(np.float32), enc, page_tokens=96)
+    fx = I.load_manifest(tmp_path)
+    m = fx["manifest"]
+    P = m["page_tokens"]
+
+    def f16(a):
+        return torch.from_numpy(np.ascontiguousarray(a, np.float16)).cuda()
+    k = contiguous_fp16_plane(f16(fx["k"]["fp16"][None]), P)
+    v = contiguous_astc_plane(torch.from_numpy(fx["v"]["blocks"][None].copy()).cuda(), f16(fx["v"]["offsets"][None, ..., 0]),
+                              f16(fx["v"]["scales"][None, ..., 0]), block=fx["v"]["block"], layout=m["layout"],
+                              normalization=fx["v"]["normalization"], head_dim=D, page_tokens=P)
+    out = Attention(torch.from_numpy(fx["q"][None]).cuda(), k, v, page_tokens=P, max_tokens=m["tokens"]).run()
+    torch.cuda.synchronize()
+    assert_attention_close(out.cpu().numpy()[0], g["attn_out"], "probe-v1 fixture vs reference codec.attention")

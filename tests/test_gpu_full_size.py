@@ -1,0 +1,193 @@
+"""GPU parity at the configurations' full token counts, on the benchmark's own
+inputs (bench.Workload: the same generators, pools and split plans the bench
+line times), against the oracle.
+
+The reference gates every timed variant on its own decoded values before it
+publishes a number (metal/probe_gqa_v10.mm:717-725, relative L2 <= 1e-4 vs
+FP64; the decode gate :741-781). Here each case rebuilds K and V on the CPU
+from the same compressed blocks (oracle decode, fp16 view, unfused fp32
+restore, codec.py:198-208), runs float64 attention (codec.py:253-267) and
+compares with the fused kernel's output: max-abs 2e-3, relative 1e-3,
+relative L2 1e-4. The blocks are tiled from pools (astcenc golden rows for
+config 2, this library's encoder for the others), so the oracle decodes each
+pool once and gathers.
+
+Set AKV_PARITY_REPORT=<file> to write each case's metrics as JSON lines.
+"""
+import json
+import math
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from common import ATOL, REL_L2, RTOL
+from oracle import oracle as O
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+pytestmark = pytest.mark.gpu
+
+
+def _pool_rows_u(blocks: np.ndarray, bs: int, layout: str) -> np.ndarray:
+    """Oracle fp16 view of pool rows [R, cols, 16] -> u [R, bs, cols*bs*comp]."""
+    R, cols, _ = blocks.shape
+    tex = O.decode_blocks(blocks.reshape(-1, 16), bs, O.OUT_FP16, threads=O.cpu_threads()).astype(np.float32)
+    tex = tex.reshape(R, cols, bs, bs, 4).transpose(0, 2, 1, 3, 4)  # [R, y, cols, x, 4]
+    if layout == "scalar":
+        return np.ascontiguousarray(tex[..., 0].reshape(R, bs, cols * bs))
+    return np.ascontiguousarray(tex.reshape(R, bs, cols * bs * 4))
+
+
+def _affine(u: np.ndarray, off: np.ndarray, scl: np.ndarray, bs: int) -> np.ndarray:
+    """Unfused fp32 restore with one (offset, scale) per bs x bs block: u [T, W]."""
+    T, W = u.shape
+    s = np.repeat(np.repeat(scl.astype(np.float32), bs, 0), bs, 1)[:T, :W]
+    o = np.repeat(np.repeat(off.astype(np.float32), bs, 0), bs, 1)[:T, :W]
+    return u * s + o
+
+
+def _attn_head(q: np.ndarray, k: np.ndarray, v: np.ndarray) -> np.ndarray:
+    """float64 softmax(q k^T / sqrt(D)) v for the query rows of one KV head."""
+    q, k, v = (np.asarray(a, np.float64) for a in (q, k, v))
+    s = q @ k.T * q.shape[-1] ** -0.5
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    return p @ v
+
+
+def _report(name: str, got: np.ndarray, ref: np.ndarray, extra: dict | None = None):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    m = {"case": name, "max_abs": float(d.max()), "rel_max": float(d.max() / max(np.abs(ref).max(), 1e-30)),
+         "rel_l2": float(np.linalg.norm(d) / max(np.linalg.norm(ref), 1e-30)), **(extra or {})}
+    print(json.dumps(m))
+    if os.environ.get("AKV_PARITY_REPORT"):
+        with open(os.environ["AKV_PARITY_REPORT"], "a") as f:
+            f.write(json.dumps(m) + "\n")
+    assert np.all(np.isfinite(got)), name
+    np.testing.assert_allclose(got, ref, atol=ATOL, rtol=RTOL, err_msg=name)
+    assert m["rel_l2"] <= REL_L2, m
+
+
+def _run(wl) -> np.ndarray:
+    out = wl.attn.run()
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_config2_full_size_bench_inputs(cuda):
+    """Config 2 as benchmarked, one sequence: T 32768, Hq32/Hkv8, bf16 q, FP16
+    K, astcenc 6x6 golden rows tiled with a random block affine, default split."""
+    import bench
+    wl = bench.Workload("c2", cuda, batch=1)
+    got = _run(wl)
+    pu = _pool_rows_u(bench.pool("c2v"), 6, "scalar")  # [R, 6, 66]
+    idx = wl.host["idx"][0].cpu().numpy()  # [H, rows, 2]
+    off, scl = wl.vp.offsets[0].cpu().numpy(), wl.vp.scales[0].cpu().numpy()
+    k = wl.kp.data[0].float().cpu().numpy()
+    q = wl.q[0].float().cpu().numpy()
+    T, D, G = wl.lens[0], 128, 4
+    ref = np.zeros((32, D))
+    for h in range(8):
+        u = np.concatenate([pu[idx[h, :, 0]], pu[idx[h, :, 1]]], axis=-1).reshape(-1, 132)
+        v = _affine(u, off[h], scl[h], 6)[:T, :D]
+        ref[h * G:(h + 1) * G] = _attn_head(q[h * G:(h + 1) * G], k[h, :T], v)
+    _report("config2 B1 T32768 (bench inputs)", got[0], ref, wl.attn.plan())
+
+
+def test_config2_fp16_control_full_size(cuda):
+    import bench
+    wl = bench.Workload("c2fp16", cuda, batch=1)
+    got = _run(wl)
+    k = wl.kp.data[0].float().cpu().numpy()
+    v = wl.vp.data[0].float().cpu().numpy()
+    q = wl.q[0].float().cpu().numpy()
+    T, G = wl.lens[0], 4
+    ref = np.concatenate([_attn_head(q[h * G:(h + 1) * G], k[h, :T], v[h, :T]) for h in range(8)])
+    _report("config2 FP16 control B1 T32768", got[0], ref, wl.attn.plan())
+
+
+def test_config3_full_size_bench_inputs(cuda):
+    """Config 3, one sequence at T 131072: ASTC 4x4 K with the 2-channel FP16
+    side plane, ASTC 8x8 V, block affine on both, Hq64/Hkv8."""
+    import bench
+    wl = bench.Workload("c3", cuda, units=[0])
+    got = _run(wl)
+    ku = _pool_rows_u(bench.pool("c3k"), 4, "scalar")  # [R, 4, 128]
+    vu = _pool_rows_u(bench.pool("c3v"), 8, "scalar")  # [R, 8, 128]
+    kidx, vidx = wl.host["kidx"][0].cpu().numpy(), wl.host["vidx"][0].cpu().numpy()
+    koff, kscl = wl.kp.offsets[0].cpu().numpy(), wl.kp.scales[0].cpu().numpy()
+    voff, vscl = wl.vp.offsets[0].cpu().numpy(), wl.vp.scales[0].cpu().numpy()
+    side = wl.kp.side[0].float().cpu().numpy()
+    ch = wl.host["side_channels"].cpu().numpy()
+    q = wl.q[0].float().cpu().numpy()
+    T, D, G = wl.lens[0], 128, 8
+    ref = np.zeros((64, D))
+    for h in range(8):
+        k = _affine(ku[kidx[h]].reshape(-1, D), koff[h], kscl[h], 4)[:T]
+        k[:, ch[h]] = side[h]
+        v = _affine(vu[vidx[h]].reshape(-1, D), voff[h], vscl[h], 8)[:T]
+        ref[h * G:(h + 1) * G] = _attn_head(q[h * G:(h + 1) * G], k, v)
+    _report("config3 B1 T131072 (bench inputs)", got[0], ref, wl.attn.plan())
+
+
+def test_config4_one_65536_token_sequence_permuted_pages(cuda):
+    """Config 4 layout with one 65536-token sequence: 256 pages of 256 tokens at
+    randomly permuted atlas positions, FP16 K pages, ASTC 4x4 V atlas."""
+    import bench
+    wl = bench.Workload("c4", cuda, units=[0], lens=[65536])
+    table = wl.table[0].cpu().numpy()
+    assert sorted(table.tolist()) == list(range(256)) and table.tolist() != list(range(256))
+    got = _run(wl)
+    pu = _pool_rows_u(bench.pool("c4v"), 4, "scalar")  # [R, 4, 128]
+    idx = wl.host["idx"].cpu().numpy()  # [atlas pages, H, 64]
+    off, scl = wl.vp.offsets.cpu().numpy(), wl.vp.scales.cpu().numpy()  # [atlas pages, H, 64, 32]
+    kp = wl.kp.data.float().cpu().numpy()  # [atlas pages, H, 256, 128]
+    q = wl.q[0].float().cpu().numpy()
+    T, D, G = 65536, 128, 4
+    ref = np.zeros((32, D))
+    for h in range(8):
+        k = kp[table, h].reshape(-1, D)[:T]
+        u = pu[idx[table, h].reshape(-1)].reshape(-1, D)
+        v = _affine(u, off[table, h].reshape(-1, 32), scl[table, h].reshape(-1, 32), 4)[:T]
+        ref[h * G:(h + 1) * G] = _attn_head(q[h * G:(h + 1) * G], k, v)
+    _report("config4 one sequence T65536, permuted pages", got[0], ref, wl.attn.plan())
+
+
+def test_config1_thirty_layers_decoded_v_bit_exact_and_attention(cuda):
+    """Config 1 at full size: 30 layers x T 8192, RGBA 4x4 V with 16-token
+    page_channel metadata. The restored V of every layer
+    (akv_cuda_restore_plane) equals the oracle's decode + unfused restore bit
+    for bit, and the 30-layer attention launch matches float64."""
+    import bench
+    from astc_kv_cuda.ops import restore_plane
+    wl = bench.Workload("c1", cuda)
+    got = _run(wl)
+    pu = _pool_rows_u(bench.pool("c1v"), 4, "rgba")  # [R, 4, 64]
+    idx = wl.host["idx"].cpu().numpy()  # [L, H, rows]
+    L, H, T, D, G = 30, 3, 8192, 64, 3
+    restored = restore_plane(wl.vp, batch=L, kv_heads=H, max_tokens=T, head_dim=D, page_tokens=16)
+    torch.cuda.synchronize()
+    off, scl = wl.vp.offsets.cpu().numpy(), wl.vp.scales.cpu().numpy()  # [L, H, pages, D]
+    kk = wl.kp.data.float().cpu().numpy()
+    q = wl.q.float().cpu().numpy()
+    ref = np.zeros((L, 9, D))
+    mismatched = 0
+    for l in range(L):
+        gpu_v = restored[l].cpu().numpy()
+        for h in range(H):
+            u = pu[idx[l, h]].reshape(T, D)
+            v = (u.reshape(T // 16, 16, D) * scl[l, h][:, None, :].astype(np.float32)
+                 + off[l, h][:, None, :].astype(np.float32)).reshape(T, D)
+            mismatched += int(np.count_nonzero(v.view(np.uint32) != gpu_v[h].view(np.uint32)))
+            ref[l, h * G:(h + 1) * G] = _attn_head(q[l, h * G:(h + 1) * G], kk[l, h], v)
+    assert mismatched == 0, f"{mismatched} restored V values differ from the oracle"
+    _report("config1 30 layers x T8192", got, ref, {**wl.attn.plan(), "restored_v_bit_exact": True})

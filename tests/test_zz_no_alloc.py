@@ -9,11 +9,14 @@ run under a fixed device-memory budget. They cannot provide the split-partial
 workspace that `akv_cuda_decode_attention` asks for, so this variant keeps
 those partials in a static device array inside the library.
 
-The test drives both entry points through the C ABI on the same descriptor
-and requires the workspace-free call to agree with the ordinary call within
-the attention tolerance of the other tests, on two calls in a row (the second
-call reuses the static array the first one left behind). It also checks that
-a descriptor needing more scratch than the array holds is refused with its
+The test drives both entry points through the C ABI on the same descriptor.
+With the same split plan both launch the same kernels, so the workspace-free
+call must reproduce the ordinary call bit for bit, on two calls in a row (the
+second call reuses the static array the first one left behind); both must
+also agree with the float64 attention over the oracle's decode of the same
+blocks within the attention tolerance of the other tests. A descriptor that
+leaves the split to the library gets a split that fits the array; one whose
+explicit split needs more scratch than the array holds is refused with its
 own status code before anything runs. The file is named to be collected
 last and builds its inputs itself, so it passes alone in a fresh process as
 well as after the rest of the suite.
@@ -24,7 +27,8 @@ import numpy as np
 import pytest
 import torch
 
-from common import ATOL, RTOL, golden
+from common import ATOL, REL_L2, RTOL, golden, oracle_restore
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -43,29 +47,76 @@ def _case():
     for p in (k, v):
         p.stride_batch = p.meta_stride_batch = 0
     rng = np.random.default_rng(77)
-    q = torch.from_numpy(rng.standard_normal((5, 9, 64)).astype(np.float32)).cuda()
-    lens = torch.tensor([384, 1, 200, 97, 383], dtype=torch.int32, device="cuda")
-    return Attention(q, k, v, page_tokens=96, max_tokens=384, seq_lens=lens, split_tokens=48)
+    qn = rng.standard_normal((5, 9, 64)).astype(np.float32)
+    q = torch.from_numpy(qn).cuda()
+    lens = [384, 1, 200, 97, 383]
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    attn = Attention(q, k, v, page_tokens=96, max_tokens=384, seq_lens=lens_t, split_tokens=48)
+    # Oracle: CPU decode of the same blocks, unfused fp32 restore, float64 attention.
+    vr = oracle_restore(g["v_blocks"], g["v_offset"], g["v_scale"], "token", 6, "scalar", 64, 96)
+    kk = g["k"].astype(np.float32)
+    expect = O.attention_f64(qn, np.broadcast_to(kk, (5,) + kk.shape), np.broadcast_to(vr, (5,) + vr.shape), lens)
+    return attn, expect
+
+
+def _noalloc(attn, split_tokens=None):
+    from astc_kv_cuda import _lib as L
+    lib = L.lib()
+    # Hand the descriptor over without any workspace.
+    d = L.AkvAttnDesc.from_buffer_copy(attn.desc)
+    d.workspace_dev, d.workspace_bytes = None, 0
+    if split_tokens is not None:
+        d.split_tokens = split_tokens
+    stream = torch.cuda.current_stream().cuda_stream or None
+    rc = lib.akv_cuda_decode_attention_noalloc(ct.byref(d), stream)
+    assert rc == 0, lib.akv_cuda_error(rc).decode()
+    torch.cuda.synchronize()
+    return attn.out.cpu().numpy()
+
+
+def _close_to(out, expect, what):
+    np.testing.assert_allclose(out, expect, atol=ATOL, rtol=RTOL, err_msg=what)
+    rel = np.linalg.norm(out - expect) / np.linalg.norm(expect)
+    assert rel <= REL_L2, f"{what}: relative L2 {rel:.3e}"
 
 
 def test_noalloc_matches_workspace_entry_point(cuda):
-    from astc_kv_cuda import _lib as L
-    lib = L.lib()
-    attn = _case()
-    ref = attn.run().clone()
+    attn, expect = _case()
+    ref = attn.run().clone().cpu().numpy()
     torch.cuda.synchronize()
-    out = attn.out
+    _close_to(ref, expect, "workspace entry point vs oracle")
     for call in range(2):
-        out.fill_(float("nan"))
-        # Hand the descriptor over without any workspace.
-        d = L.AkvAttnDesc.from_buffer_copy(attn.desc)
-        d.workspace_dev, d.workspace_bytes = None, 0
-        stream = torch.cuda.current_stream().cuda_stream or None
-        rc = lib.akv_cuda_decode_attention_noalloc(ct.byref(d), stream)
-        assert rc == 0, lib.akv_cuda_error(rc).decode()
-        torch.cuda.synchronize()
-        np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), atol=ATOL, rtol=RTOL,
-                                   err_msg=f"call {call}")
+        attn.out.fill_(float("nan"))
+        out = _noalloc(attn)
+        # Same kernels, same split plan: identical results.
+        assert np.array_equal(out, ref), f"call {call}: differs from the workspace entry point"
+        _close_to(out, expect, f"call {call} vs oracle")
+
+
+def test_noalloc_default_split_fits_the_static_array(cuda):
+    """split_tokens = 0 leaves the split to the library, which then picks one
+    whose partials fit the static array; the result still matches the oracle.
+    The second case is config 2's shape (Hq32/Hkv8, D128) at one sequence of
+    32768 tokens, whose usual split would need about 11 MB of partials."""
+    attn, expect = _case()
+    for call in range(2):
+        attn.out.fill_(float("nan"))
+        out = _noalloc(attn, split_tokens=0)
+        _close_to(out, expect, f"default split, call {call}")
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from astc_kv_cuda import _lib as L
+    wl = bench.Workload("c2", cuda, batch=1)
+    assert wl.attn.workspace.numel() * 4 > L.AKV_STATIC_WORKSPACE_BYTES
+    ref = wl.attn.run().clone().cpu().numpy()
+    for call in range(2):
+        wl.attn.out.fill_(float("nan"))
+        out = _noalloc(wl.attn, split_tokens=0)
+        np.testing.assert_allclose(out, ref, atol=ATOL, rtol=RTOL, err_msg=f"config 2 shape, call {call}")
+        rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+        assert rel <= REL_L2, rel
 
 
 def test_noalloc_rejects_scratch_beyond_its_maximum(cuda):
