@@ -18,7 +18,7 @@ AKV_LAYOUT_SCALAR, AKV_LAYOUT_RGBA = 0, 1
 AKV_NORM_PAGE_CHANNEL, AKV_NORM_TOKEN, AKV_NORM_BLOCK_AFFINE = 0, 1, 2
 AKV_Q_F32, AKV_Q_BF16, AKV_Q_F16 = 0, 1, 2
 AKV_PHASE_SPLIT, AKV_PHASE_MERGE = 1, 2
-AKV_KERNEL_GENERIC, AKV_KERNEL_FAST = 0, 1
+AKV_KERNEL_GENERIC, AKV_KERNEL_FAST, AKV_KERNEL_FP16 = 0, 1, 2
 AKV_ERR_STATIC_WORKSPACE = 8
 AKV_STATIC_WORKSPACE_BYTES = 8 << 20
 

@@ -278,7 +278,8 @@ class Attention:
         """The launch plan (akv_cuda_attention_plan): kernel name, split size, splits."""
         k, sp, ns = ct.c_int(), ct.c_int(), ct.c_int()
         L.check(L.lib().akv_cuda_attention_plan(self._dref, ct.byref(k), ct.byref(sp), ct.byref(ns)), "attention_plan")
-        return {"kernel": "attn_fast_kernel" if k.value == L.AKV_KERNEL_FAST else "attn_split_kernel",
+        names = {L.AKV_KERNEL_FAST: "attn_fast_kernel", L.AKV_KERNEL_FP16: "attn_fp16_kernel"}
+        return {"kernel": names.get(k.value, "attn_split_kernel"),
                 "split_tokens": sp.value, "nsplits": ns.value}
 
     def run_phase(self, phase: int, stream: torch.cuda.Stream | None = None) -> None:

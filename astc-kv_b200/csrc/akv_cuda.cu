@@ -14,6 +14,7 @@
 #include "../../include/akv_cuda.h"
 #include "akv_attention_kernels.cuh"
 #include "akv_attn_fast.cuh"
+#include "akv_attn_fp16.cuh"
 #include "akv_decode_kernels.cuh"
 #include "akv_tables.h"
 
@@ -188,6 +189,64 @@ const FastVariant kFastVariants[] = {
 };
 #undef AKV_FAST
 
+template <int D, int G>
+int launch_fp16(const AttnParams& p, cudaStream_t s, int phases) {
+    using C = f16k::Cfg<D, G>;
+    auto kern = f16k::attn_fp16_kernel<D, G>;
+    const size_t smem = sizeof(f16k::Smem<D, G>);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess) {
+        cudaGetLastError();
+        return AKV_ERR_CUDA;
+    }
+    if (phases & AKV_PHASE_SPLIT) {
+        dim3 grid(p.nsplits, p.Hkv, p.B);
+        kern<<<grid, C::THREADS, smem, s>>>(p);
+        if (int st = launch_status()) return st;
+    }
+    if (phases & AKV_PHASE_MERGE) {
+        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        if (int st = launch_status()) return st;
+    }
+    return AKV_OK;
+}
+
+struct Fp16Variant {
+    int D, G;
+    Launcher fn;
+    size_t smem;
+};
+
+// FP16 K + FP16 V (the FP16 control) on the tensor-core kernel.
+#define AKV_FP16(D, G) {D, G, &launch_fp16<D, G>, sizeof(f16k::Smem<D, G>)}
+const Fp16Variant kFp16Variants[] = {AKV_FP16(64, 3), AKV_FP16(128, 4), AKV_FP16(128, 8)};
+#undef AKV_FP16
+
+const Fp16Variant* find_fp16(int D, int G) {
+    for (const Fp16Variant& v : kFp16Variants)
+        if (v.D == D && v.G == G) return &v;
+    return nullptr;
+}
+
+bool fp16_path_ok(const AkvAttnDesc* d) {
+    const char* env = std::getenv("AKV_ATTN_PATH");
+    if (env && std::strcmp(env, "generic") == 0) return false;
+    if (d->k.storage != AKV_STORAGE_FP16 || d->v.storage != AKV_STORAGE_FP16) return false;
+    const Fp16Variant* fv = find_fp16(d->head_dim, d->q_heads / d->kv_heads);
+    if (!fv) return false;
+    int dev = 0, smem_max = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        fv->smem > static_cast<size_t>(smem_max)) {
+        cudaGetLastError();
+        return false;
+    }
+    // One bulk copy per row: every row start 16-byte aligned.
+    const AkvPlane* planes[2] = {&d->k, &d->v};
+    for (const AkvPlane* pl : planes)
+        if (pl->stride_batch % 16 || pl->stride_head % 16 || pl->stride_page % 16) return false;
+    return true;
+}
+
 int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : (kbs ? 32 : 64); }
 
 const FastVariant* find_fast(int D, int G, int vbs, int kbs, int vl) {
@@ -294,7 +353,7 @@ const Variant* find_variant(int D, int G, int kbs, int vbs, int vl) {
 
 struct AttnPlan {
     int kbs, vbs, vl, split, nsplits;
-    bool fast;
+    int kernel;  // AKV_KERNEL_*
     size_t ws;
 };
 
@@ -338,7 +397,9 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out, size_t ws_limit = 0) {
     out->vl = d->v.storage == AKV_STORAGE_ASTC ? d->v.layout : AKV_LAYOUT_SCALAR;
     if (!find_variant(d->head_dim, d->q_heads / d->kv_heads, out->kbs, out->vbs, out->vl)) return AKV_ERR_UNSUPPORTED;
     const bool fast_shape = out->vbs && find_fast(d->head_dim, d->q_heads / d->kv_heads, out->vbs, out->kbs, out->vl);
-    const int ch = fast_shape ? fast_chunk(out->kbs, out->vbs) : chunk_tokens(out->kbs, out->vbs);
+    const bool fp16_shape = !out->vbs && !out->kbs && find_fp16(d->head_dim, d->q_heads / d->kv_heads);
+    const int ch = fast_shape ? fast_chunk(out->kbs, out->vbs)
+                              : (fp16_shape ? f16k::Cfg<64, 3>::CH : chunk_tokens(out->kbs, out->vbs));
     int split = d->split_tokens;
     if (split <= 0) {
         // Enough (split, head, batch) units for ~64 CTAs per SM: many short
@@ -376,7 +437,8 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out, size_t ws_limit = 0) {
     if (split % lcm_fp) return AKV_ERR_INVALID_ARGUMENT;
     out->split = split;
     out->nsplits = (d->max_tokens + split - 1) / split;
-    out->fast = fast_path_ok(d, out->kbs, out->vbs, out->vl, split);
+    out->kernel = fast_path_ok(d, out->kbs, out->vbs, out->vl, split) ? AKV_KERNEL_FAST
+                  : (fp16_shape && fp16_path_ok(d)) ? AKV_KERNEL_FP16 : AKV_KERNEL_GENERIC;
     out->ws = static_cast<size_t>(d->batch) * d->q_heads * out->nsplits * (d->head_dim + 2) * sizeof(float);
     return AKV_OK;
 }
@@ -444,7 +506,9 @@ AttnParams segment_params(const AkvAttnDesc* d, const AttnPlan& plan, const AkvA
 }
 
 int launch_segment(const AkvAttnDesc* d, const AttnPlan& plan, const AttnParams& p, cudaStream_t s, int phase) {
-    if (plan.fast) return find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs, plan.vl)->fn(p, s, phase);
+    if (plan.kernel == AKV_KERNEL_FAST)
+        return find_fast(d->head_dim, d->q_heads / d->kv_heads, plan.vbs, plan.kbs, plan.vl)->fn(p, s, phase);
+    if (plan.kernel == AKV_KERNEL_FP16) return find_fp16(d->head_dim, d->q_heads / d->kv_heads)->fn(p, s, phase);
     return find_variant(d->head_dim, d->q_heads / d->kv_heads, plan.kbs, plan.vbs, plan.vl)->fn(p, s, phase);
 }
 
@@ -537,7 +601,7 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc) {
 int akv_cuda_attention_plan(const AkvAttnDesc* desc, int* kernel, int* split_tokens, int* nsplits) {
     AttnPlan plan;
     if (int st = plan_attention(desc, &plan)) return st;
-    if (kernel) *kernel = plan.fast ? AKV_KERNEL_FAST : AKV_KERNEL_GENERIC;
+    if (kernel) *kernel = plan.kernel;
     if (split_tokens) *split_tokens = plan.split;
     if (nsplits) *nsplits = plan.nsplits;
     return AKV_OK;

@@ -153,13 +153,6 @@ typedef struct AkvAttnDesc {
 /* Workspace bytes the descriptor needs (0 on invalid descriptors). */
 size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc);
 
-/* The launch plan of a descriptor, without launching: which split kernel
- * runs (AKV_KERNEL_FAST: fused decode + tensor-core kernel for scalar ASTC V
- * with whole chunks per page and 16-byte aligned metadata; AKV_KERNEL_GENERIC
- * otherwise), the split size in tokens and the number of splits. Any output
- * pointer may be NULL. Returns the status akv_cuda_decode_attention would
- * return for a descriptor error. No counterpart in the reference (its Metal
- * host picks kernels in the probe programs). */
 /*
  * Decode attention over two KV segments in one softmax: `desc` (for example
  * the ASTC-compressed complete pages) and `tail` (for example the exact
@@ -176,8 +169,18 @@ size_t akv_cuda_attention_workspace(const AkvAttnDesc* desc);
 size_t akv_cuda_attention_tail_workspace(const AkvAttnDesc* desc, const AkvAttnDesc* tail);
 int akv_cuda_decode_attention_tail(const AkvAttnDesc* desc, const AkvAttnDesc* tail, void* stream);
 
+/* The launch plan of a descriptor, without launching: which split kernel
+ * runs (AKV_KERNEL_FAST: fused decode + tensor-core kernel for scalar ASTC V
+ * with whole chunks per page and 16-byte aligned metadata; AKV_KERNEL_FP16:
+ * tensor-core kernel for FP16 K with FP16 V, the FP16 control;
+ * AKV_KERNEL_GENERIC otherwise), the split size in tokens and the number of
+ * splits. Any output pointer may be NULL. Returns the status
+ * akv_cuda_decode_attention would return for a descriptor error. No
+ * counterpart in the reference (its Metal host picks kernels in the probe
+ * programs). */
 #define AKV_KERNEL_GENERIC 0
 #define AKV_KERNEL_FAST 1
+#define AKV_KERNEL_FP16 2
 int akv_cuda_attention_plan(const AkvAttnDesc* desc, int* kernel, int* split_tokens, int* nsplits);
 
 int akv_cuda_decode_attention(const AkvAttnDesc* desc, void* stream);

@@ -299,3 +299,28 @@ def test_rgba_pages_smaller_than_a_chunk_with_a_partial_last_chunk(cuda):
         kp = contiguous_fp16_plane(torch.zeros(1, 3, T, 64, dtype=torch.float16, device="cuda"), 16)
         q = torch.zeros(1, 9, 64, device="cuda")
         assert Attention(q, kp, vp, page_tokens=16, max_tokens=T).plan()["kernel"] == kernel, T
+
+
+@pytest.mark.parametrize("D,G,T,P,split,lens", [(128, 4, 1000, 96, 0, [1000, 999, 64, 1]), (64, 3, 384, 16, 48, [384, 7]),
+                                                  (128, 8, 512, 64, 200, [512, 130])])
+def test_fp16_control_kernel(cuda, D, G, T, P, split, lens):
+    """FP16 K + FP16 V takes the tensor-core FP16 kernel (per-row bulk copies,
+    chunks that cross pages, ragged and partial last chunks, splits that are
+    not whole chunks) and matches float64 attention."""
+    from astc_kv_cuda.ops import Attention, contiguous_fp16_plane
+    rng = np.random.default_rng(D + G + T)
+    Hkv, B = 2, len(lens)
+    k = (rng.standard_normal((B, Hkv, T, D)) * 0.8).astype(np.float16)
+    v = (rng.standard_normal((B, Hkv, T, D)) * 2.0).astype(np.float16)
+    q = rng.standard_normal((B, Hkv * G, D)).astype(np.float32)
+    Tc = -(-T // P) * P
+    kp = np.zeros((B, Hkv, Tc, D), np.float16)
+    vp = np.zeros_like(kp)
+    kp[:, :, :T], vp[:, :, :T] = k, v
+    attn = Attention(torch.from_numpy(q).cuda(), contiguous_fp16_plane(f16t(kp), P), contiguous_fp16_plane(f16t(vp), P),
+                     page_tokens=P, max_tokens=T, seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"),
+                     split_tokens=split)
+    assert attn.plan()["kernel"] == "attn_fp16_kernel"
+    got = attn.run().cpu().numpy()
+    ref = O.attention_f64(q, k.astype(np.float32), v.astype(np.float32), lens)
+    assert_attention_close(got, ref, f"fp16 control D{D} G{G} T{T}")
