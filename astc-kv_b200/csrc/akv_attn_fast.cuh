@@ -400,6 +400,76 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
         const int ncol = min(BS, D - col0);
         const float sc = affine ? __half2float(mscl[i]) : 0.f;
         const float of = affine ? __half2float(moff[i]) : 0.f;
+        if constexpr (BS == 6) {
+            // The table-driven header path: luminance blocks with a 6x6 grid
+            // (value table, then the texels) or a reduced grid (descriptor
+            // slot for phases 1a / 1b), and constant blocks.
+            const uint32_t f6 = __ldg(&g_f6.info[blk.x & 0x1FFFu]);
+            bool cst = (f6 & kF6Const) != 0, lum = false;
+            if (f6 & kF6Lum) {
+                const bool cem0 = (blk.x & 0x1800u) == 0 ? ((blk.x >> 13) & 15) == 0 : ((blk.x >> 23) & 0x3F) == 0;
+                if (cem0) {
+                    cst = (f6 & kF6Err) != 0;
+                    lum = !cst;
+                }
+            }
+            if (cst) {
+                ds.tab[0][tid] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
+                const uint32_t zero[9] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+                write6<LD>(zero, &ds.tab[0][tid], NC, norm, moff, mscl, row0, col0, thi, tlo);
+                continue;
+            }
+            if (lum) {
+                F6Lum o;
+                decode_f6_lum(blk, f6, &ds.codes[0][tid], NC, o);
+                if (f6 & kF6Full) {
+                    uint32_t idx[9];
+                    f6_entries(blk, o, idx);
+                    build_table(o.v, o.parts, o.wq, o.L, affine, sc, of, &ds.tab[0][tid], NC);
+                    write6<LD>(idx, &ds.tab[0][tid], NC, norm, moff, mscl, row0, col0, thi, tlo);
+                    continue;
+                }
+                // Reduced grid: a descriptor slot, its grid codes in this
+                // thread's code column for the late weight expansion.
+                const int slot = atomicAdd(&ds.nslot, 1);
+                if (slot >= kCap) {
+                    eval_block_generic<BS, LD>(blk, norm, sc, of, moff, mscl, row0, col0, rows, ncol, thi, tlo);
+                    continue;
+                }
+                const uint32_t me6 = __ldg(&g_akv_tables.mode[1][blk.x & 0x7FFu]);
+                const int wx = mode_wx(me6), wy = mode_wy(me6);
+                BlockDesc<1>& d = ds.desc[slot];
+                if (o.parts > 1) {
+                    const uint32_t* pt = g_akv_tables.part[1][o.parts - 2][(blk.x >> 13) & 0x3FF];
+                    d.pat[0] = __ldg(pt); d.pat[1] = __ldg(pt + 1);
+                    d.pat_hi[0] = __ldg(pt + 2); d.pat_hi[1] = __ldg(pt + 3);
+                } else {
+                    d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0u;
+                }
+                d.ep[0] = static_cast<uint32_t>(o.v[0] | (o.v[2] << 8) | (o.v[4] << 16) | (o.v[6] << 24));
+                d.ep[1] = static_cast<uint32_t>(o.v[1] | (o.v[3] << 8) | (o.v[5] << 16) | (o.v[7] << 24));
+                d.info = static_cast<uint32_t>(o.parts - 1) | (1u << kInfoReduced) |
+                         (static_cast<uint32_t>(wx) << kInfoWx) | (static_cast<uint32_t>(wy) << kInfoWy);
+                uint8_t* cc = &ds.codes[0][tid];
+                const int count = wx * wy;
+#pragma unroll
+                for (int j = 0; j < 36; ++j)
+                    if (j < count) cc[j * NC] = static_cast<uint8_t>(byte_of(o.cw, j));
+                ds.slot_pos[slot] = static_cast<uint32_t>(row0) | (static_cast<uint32_t>(col0) << 16) | kSlotRows;
+                ds.slot_aff[slot] = make_float2(sc, of);
+                if (late_w) {
+                    ds.slot_src[slot] = static_cast<uint32_t>(tid) | (static_cast<uint32_t>(o.wq) << 16);
+                } else {
+                    const uint8_t* un = g_akv_tables.wunq[o.wq];
+                    for (int r = 0; r < wy; ++r) {
+#pragma unroll
+                        for (int c = 0; c < BS; ++c)
+                            if (c < wx) ds.w[slot][8 * r + c] = desc_weight(cc, NC, un, wx, 8 * r + c);
+                    }
+                }
+                continue;
+            }
+        }
         uint32_t me;
         int cq;
         const int kind = block_kind<BS>(blk, me, cq);
@@ -1047,9 +1117,12 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         return;
     }
 
-    // Merge the MMA warps' (m, l, O) into one split partial.
-    float* red = reinterpret_cast<float*>(&sm.vhi[0][0]);  // G * D floats, fits in the V tiles
-    for (int i = tid; i < G * D; i += THREADS) red[i] = 0.f;
+    // Merge the MMA warps' (m, l, O) into one split partial: each warp
+    // stores its rescaled O (its token tile, its dim half), then the token
+    // tiles are summed in a fixed order (the result does not depend on warp
+    // timing).
+    float* red = reinterpret_cast<float*>(&sm.vhi[0][0]);  // [NWM][G][D] floats
+    static_assert(sizeof(float) * NWM * G * D <= sizeof(sm.vhi), "merge buffer fits the V tile");
     if (dh == 0 && lane < 4) {
         sm.wm[tw][2 * lane] = m_run[0];
         sm.wm[tw][2 * lane + 1] = m_run[1];
@@ -1067,22 +1140,27 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
             for (int w = 0; w < NWM; ++w) M = fmaxf(M, sm.wm[w][hh]);
             scl[j] = (M == -CUDART_INF_F || m_run[j] == -CUDART_INF_F) ? 0.f : exp2f(m_run[j] - M);
         }
+        float* mine = red + tw * G * D;
 #pragma unroll
         for (int mt = 0; mt < KH; ++mt) {
             const int d0 = 16 * (dh * KH + mt) + qn;
             if (2 * qj < G) {
-                atomicAdd(&red[(2 * qj) * D + d0], o[mt][0] * scl[0]);
-                atomicAdd(&red[(2 * qj) * D + d0 + 8], o[mt][2] * scl[0]);
+                mine[(2 * qj) * D + d0] = o[mt][0] * scl[0];
+                mine[(2 * qj) * D + d0 + 8] = o[mt][2] * scl[0];
             }
             if (2 * qj + 1 < G) {
-                atomicAdd(&red[(2 * qj + 1) * D + d0], o[mt][1] * scl[1]);
-                atomicAdd(&red[(2 * qj + 1) * D + d0 + 8], o[mt][3] * scl[1]);
+                mine[(2 * qj + 1) * D + d0] = o[mt][1] * scl[1];
+                mine[(2 * qj + 1) * D + d0 + 8] = o[mt][3] * scl[1];
             }
         }
     }
     __syncthreads();
-    for (int i = tid; i < G * D; i += THREADS)
-        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = red[i];
+    for (int i = tid; i < G * D; i += THREADS) {
+        float acc = red[i];
+#pragma unroll
+        for (int w = 1; w < NWM; ++w) acc += red[w * G * D + i];
+        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = acc;
+    }
     if (tid < G) {
         float M = -CUDART_INF_F;
         for (int w = 0; w < NWM; ++w) M = fmaxf(M, sm.wm[w][tid]);

@@ -5,35 +5,42 @@
 // Per CTA: one (split, kv head, batch) unit, processed in chunks of CH = 64
 // tokens, one warp per 16-token tile.
 //
-//   * Staging: the lanes of warp 0 issue one 1D bulk copy (cp.async.bulk)
-//     per K row and per V row of a chunk into padded shared-memory rows
-//     (D + 8 halves, so ldmatrix rows fall on distinct banks), three chunks
-//     ahead in a three-stage ring; each lane arrives on the stage's mbarrier
-//     with the bytes it issued. Rows past the split's last token and rows of
-//     unmapped pages are zero-filled by the same lanes before they arrive.
-//     A row's page is looked up per row, so chunks may cross pages.
+//   * Staging: every thread issues 16-byte asynchronous copies (cp.async,
+//     zero-fill form) of K and V rows into padded shared-memory rows (D + 8
+//     halves, so ldmatrix rows fall on distinct banks), two chunks ahead in a
+//     three-stage ring (commit / wait groups). Rows past the split's last
+//     token and rows of unmapped pages copy zero bytes, i.e. read as zeros.
+//     A row's page is looked up per row, so chunks may cross pages. (One 1D
+//     bulk copy per 256-byte row was measured first: the copy engine then
+//     sustains about 1.8 TB/s, a quarter of HBM, for lack of bytes per
+//     request.)
 //   * Tensor cores (mma.sync m16n8k16, fp32 accumulation): S^T = K . Q^T
 //     with q split into fp16 hi + lo (K is exact in fp16), online softmax in
 //     base 2, O^T += V^T . P^T with P split into hi + lo (V is exact), so
 //     the only rounding left is fp32 accumulation.
 //   * The warps merge their (m, l, O) at the end into one split partial, the
-//     workspace format merge_kernel reads.
+//     workspace format merge_kernel reads, summing in a fixed order (the
+//     result does not depend on warp timing).
 #pragma once
 #include "akv_attn_fast.cuh"
 
 namespace akv {
 namespace f16k {
 
-using fast::bulk_g2s;
-using fast::fence_mbar_init;
-using fast::fence_proxy_async;
 using fast::ldsm_x4;
 using fast::ldsm_x4_t;
-using fast::mbar_arrive_expect_tx;
-using fast::mbar_init;
-using fast::mbar_wait;
 using fast::mma16816;
+using fast::smem_u32;
 using fast::split_pair;
+
+// 16-byte global -> shared asynchronous copy; `bytes` 0 writes zeros (the
+// source is then not read).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int D, int G>
 struct Cfg {
@@ -43,14 +50,14 @@ struct Cfg {
     static constexpr int STAGES = 3;
     static constexpr int LD = D + 8;         // halves per staged row
     static constexpr int KS = D / 16;        // k-steps of the score MMA, dim tiles of the output
-    static constexpr int RPL = CH / 32;      // rows each producer lane stages per plane
-    static_assert(D % 16 == 0 && G <= 8 && CH % 32 == 0, "shape");
+    static constexpr int PPR = D / 8;        // 16-byte pieces per row
+    static constexpr int PPT = CH * PPR / THREADS;  // pieces per thread per plane and chunk
+    static_assert(D % 16 == 0 && G <= 8 && (CH * PPR) % THREADS == 0 && THREADS % PPR == 0, "shape");
 };
 
 template <int D, int G>
 struct Smem {
     using C = Cfg<D, G>;
-    uint64_t full[C::STAGES];
     __align__(16) __half k[C::STAGES][C::CH][C::LD];
     __align__(16) __half v[C::STAGES][C::CH][C::LD];
     __align__(16) uint4 qfrag[C::KS][32];     // per lane: q hi (2 words) | q lo (2 words)
@@ -88,56 +95,30 @@ __global__ void __launch_bounds__(Cfg<D, G>::THREADS, 2) attn_fp16_kernel(AttnPa
     const int nchunks = (t_end - t_begin + CH - 1) / CH;
     const int P = p.page_tokens;
 
-    if (tid == 0) {
-#pragma unroll
-        for (int s = 0; s < STAGES; ++s) mbar_init(&sm.full[s], 32);
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    // Producer (the 32 lanes of warp 0): chunk c -> stage s. Lane l stages
-    // rows l, l + 32, ...; each lane arrives once with its own byte count.
+    // Chunk c -> stage s: thread i copies pieces i, i + THREADS, ... of each
+    // plane (row = piece / PPR, so THREADS / PPR threads share a row).
     const uint8_t* kbase = p.k.data + b * p.k.sB + h * p.k.sH;
     const uint8_t* vbase = p.v.data + b * p.v.sB + h * p.v.sH;
     auto issue = [&](int c, int s) {
         const int t0 = t_begin + c * CH;
-        const uint8_t* ks[C::RPL];
-        const uint8_t* vs[C::RPL];
-        uint32_t bytes = 0;
 #pragma unroll
-        for (int i = 0; i < C::RPL; ++i) {
-            const int r = lane + 32 * i, t = t0 + r;
+        for (int i = 0; i < C::PPT; ++i) {
+            const int piece = tid + i * THREADS;
+            const int r = piece / C::PPR, j = piece % C::PPR;
+            const int t = t0 + r;
             const int phys = t < t_end ? phys_page(p.table, p.pps, p.num_pages, b, t / P, p.status) : -1;
-            ks[i] = vs[i] = nullptr;
-            if (phys >= 0) {
-                const int64_t off = static_cast<int64_t>(phys) * p.k.sP + static_cast<int64_t>(t % P) * (D * 2);
-                const int64_t offv = static_cast<int64_t>(phys) * p.v.sP + static_cast<int64_t>(t % P) * (D * 2);
-                ks[i] = kbase + off;
-                vs[i] = vbase + offv;
-                bytes += 2 * D * 2;
-            } else {
-                // Past the split or an unmapped page: zeros (an unmapped
-                // page's tokens read as zero K and V; later rows are masked).
-                uint4* kr = reinterpret_cast<uint4*>(&sm.k[s][r][0]);
-                uint4* vr = reinterpret_cast<uint4*>(&sm.v[s][r][0]);
-#pragma unroll
-                for (int j = 0; j < D / 8; ++j) kr[j] = vr[j] = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        mbar_arrive_expect_tx(&sm.full[s], bytes);
-#pragma unroll
-        for (int i = 0; i < C::RPL; ++i) {
-            if (ks[i]) {
-                const int r = lane + 32 * i;
-                bulk_g2s(&sm.k[s][r][0], ks[i], D * 2, &sm.full[s]);
-                bulk_g2s(&sm.v[s][r][0], vs[i], D * 2, &sm.full[s]);
-            }
+            const int64_t row = static_cast<int64_t>(t % P) * (D * 2) + j * 16;
+            const uint8_t* ks = phys >= 0 ? kbase + static_cast<int64_t>(phys) * p.k.sP + row : kbase;
+            const uint8_t* vs = phys >= 0 ? vbase + static_cast<int64_t>(phys) * p.v.sP + row : vbase;
+            const uint32_t n = phys >= 0 ? 16u : 0u;
+            cp_async16(&sm.k[s][r][8 * j], ks, n);
+            cp_async16(&sm.v[s][r][8 * j], vs, n);
         }
     };
-    if (warp == 0) {
 #pragma unroll
-        for (int c = 0; c < STAGES; ++c)
-            if (c < nchunks) issue(c, c);
+    for (int c = 0; c < STAGES - 1; ++c) {
+        if (c < nchunks) issue(c, c);
+        cp_async_commit();
     }
 
     // Query fragments (B operand of the score MMA, hi + lo) for heads
@@ -165,19 +146,19 @@ __global__ void __launch_bounds__(Cfg<D, G>::THREADS, 2) attn_fp16_kernel(AttnPa
 #pragma unroll
     for (int i = 0; i < KS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F}, l_run[2] = {0.f, 0.f};
-    int stuck = -1;
     const int mi = lane >> 3, rr = lane & 7;
 
     for (int c = 0; c < nchunks; ++c) {
         const int s = c % STAGES;
-        const uint32_t parity = (c / STAGES) & 1;
         const int t0 = t_begin + c * CH;
         const int n = min(CH, t_end - t0);
-        const bool waited = mbar_wait(&sm.full[s], parity);
-        if (__syncthreads_or(!waited)) {
-            stuck = c;
-            break;
-        }
+        // This thread's copies of chunk c have landed; the barrier makes
+        // everyone's visible and frees the stage chunk c - 1 used, which
+        // then takes chunk c + STAGES - 1.
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        if (c + STAGES - 1 < nchunks) issue(c + STAGES - 1, (c + STAGES - 1) % STAGES);
+        cp_async_commit();
         // S^T[token][head] for this warp's 16 tokens.
         float sa[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         {
@@ -255,29 +236,14 @@ __global__ void __launch_bounds__(Cfg<D, G>::THREADS, 2) attn_fp16_kernel(AttnPa
             }
         }
         __syncwarp();
-        __syncthreads();  // stage s and the P buffers are free
-        if (warp == 0 && c + STAGES < nchunks) {
-            fence_proxy_async();
-            issue(c + STAGES, s);
-        }
     }
+    cp_async_wait<0>();
+    __syncthreads();  // every stage and P buffer is free
 
-    if (stuck >= 0) {
-        // A copy never completed: report it, give every copy still in flight
-        // (chunks stuck .. stuck + STAGES - 1, one per stage) a bounded grace
-        // period so none lands after the CTA exits, and leave the split empty.
-        if (tid == 0) {
-            if (p.status) atomicExch(p.status, AKV_ERR_TIMEOUT);
-            for (int c = stuck; c < nchunks && c < stuck + STAGES; ++c) mbar_wait(&sm.full[c % STAGES], (c / STAGES) & 1);
-        }
-        __syncthreads();
-        write_empty();
-        return;
-    }
-
-    // Merge the warps' (m, l, O) into one split partial.
-    float* red = reinterpret_cast<float*>(&sm.k[0][0][0]);  // G * D floats
-    for (int i = tid; i < G * D; i += THREADS) red[i] = 0.f;
+    // Merge the warps' (m, l, O) into one split partial: each warp stores its
+    // rescaled O, then the per-warp values are summed in warp order.
+    float* red = reinterpret_cast<float*>(&sm.k[0][0][0]);  // [NW][G][D] floats
+    static_assert(sizeof(float) * NW * G * D <= sizeof(sm.k), "merge buffer fits the K stages");
     if (lane < 4) {
         sm.wm[warp][2 * lane] = m_run[0];
         sm.wm[warp][2 * lane + 1] = m_run[1];
@@ -295,22 +261,27 @@ __global__ void __launch_bounds__(Cfg<D, G>::THREADS, 2) attn_fp16_kernel(AttnPa
             for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][hh]);
             scl[j] = (M == -CUDART_INF_F || m_run[j] == -CUDART_INF_F) ? 0.f : exp2f(m_run[j] - M);
         }
+        float* mine = red + warp * G * D;
 #pragma unroll
         for (int dt = 0; dt < KS; ++dt) {
             const int d0 = 16 * dt + qn;
             if (2 * qj < G) {
-                atomicAdd(&red[(2 * qj) * D + d0], o[dt][0] * scl[0]);
-                atomicAdd(&red[(2 * qj) * D + d0 + 8], o[dt][2] * scl[0]);
+                mine[(2 * qj) * D + d0] = o[dt][0] * scl[0];
+                mine[(2 * qj) * D + d0 + 8] = o[dt][2] * scl[0];
             }
             if (2 * qj + 1 < G) {
-                atomicAdd(&red[(2 * qj + 1) * D + d0], o[dt][1] * scl[1]);
-                atomicAdd(&red[(2 * qj + 1) * D + d0 + 8], o[dt][3] * scl[1]);
+                mine[(2 * qj + 1) * D + d0] = o[dt][1] * scl[1];
+                mine[(2 * qj + 1) * D + d0 + 8] = o[dt][3] * scl[1];
             }
         }
     }
     __syncthreads();
-    for (int i = tid; i < G * D; i += THREADS)
-        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = red[i];
+    for (int i = tid; i < G * D; i += THREADS) {
+        float acc = red[i];
+#pragma unroll
+        for (int w = 1; w < NW; ++w) acc += red[w * G * D + i];
+        p.part_acc[(unit0 + static_cast<int64_t>(i / D) * p.split_stride) * D + i % D] = acc;
+    }
     if (tid < G) {
         float M = -CUDART_INF_F;
         for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][tid]);

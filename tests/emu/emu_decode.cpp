@@ -228,3 +228,92 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
     }
     return 0;
 }
+
+// The attention kernel's 6x6 table-driven header path (decode_plane's block
+// phase for 6x6 planes): constant blocks, luminance blocks with a full grid
+// (value table of unit values + per-texel entry bytes, read back as write6
+// reads them) or a reduced grid (descriptor, then desc_seg_c16 as phase 1b
+// evaluates it); anything else takes the runtime path (fast_r_one).
+// cls: 10 constant, 11 full-grid table, 12 reduced-grid descriptor, else the
+// runtime path's kind.
+extern "C" int emu_decode_f6(const uint8_t* blocks, int64_t n, float* out, int* cls) {
+    static bool ready = false;
+    if (!ready) {
+        akv::build_tables(&akv::g_akv_tables);
+        akv::build_fast6_tables(akv::g_akv_tables, &akv::fast::g_f6);
+        ready = true;
+    }
+    namespace F = akv::fast;
+    for (int64_t i = 0; i < n; ++i) {
+        uint4 blk;
+        std::memcpy(&blk, blocks + 16 * i, 16);
+        float* o = out + i * 36;
+        const uint32_t f6 = F::g_f6.info[blk.x & 0x1FFFu];
+        bool cst = (f6 & akv::kF6Const) != 0, lum = false;
+        if (f6 & akv::kF6Lum) {
+            const bool cem0 = (blk.x & 0x1800u) == 0 ? ((blk.x >> 13) & 15) == 0 : ((blk.x >> 23) & 0x3F) == 0;
+            if (cem0) {
+                cst = (f6 & akv::kF6Err) != 0;
+                lum = !cst;
+            }
+        }
+        if (cst) {
+            cls[i] = 10;
+            const float u = akv::c16_to_unit(F::const_c16(blk));
+            for (int t = 0; t < 36; ++t) o[t] = u;
+            continue;
+        }
+        if (!lum) {
+            const int rc = fast_r_one<6>(blk, cls + i, o);
+            if (rc) return rc;
+            continue;
+        }
+        uint8_t cscr[40];
+        std::memset(cscr, 0xEE, sizeof(cscr));
+        F::F6Lum d6;
+        F::decode_f6_lum(blk, f6, cscr, 1, d6);
+        if (f6 & akv::kF6Full) {
+            cls[i] = 11;
+            uint32_t idx[9];
+            F::f6_entries(blk, d6, idx);
+            uint32_t tab[F::kTabCapMax];
+            std::memset(tab, 0xEE, sizeof(tab));
+            F::build_table(d6.v, d6.parts, d6.wq, d6.L, false, 0.f, 0.f, tab, 1);
+            for (int t = 0; t < 36; ++t) {
+                const uint32_t e = F::byte_of(idx, t);
+                if (e >= static_cast<uint32_t>(d6.parts * d6.L)) return 4;
+                o[t] = __uint_as_float(tab[e]);
+            }
+            continue;
+        }
+        cls[i] = 12;
+        const uint32_t me = akv::g_akv_tables.mode[1][blk.x & 0x7FFu];
+        const int wx = akv::mode_wx(me), wy = akv::mode_wy(me);
+        akv::BlockDesc<1> d;
+        if (d6.parts > 1) {
+            const uint32_t* pt = akv::g_akv_tables.part[1][d6.parts - 2][(blk.x >> 13) & 0x3FF];
+            d.pat[0] = pt[0]; d.pat[1] = pt[1]; d.pat_hi[0] = pt[2]; d.pat_hi[1] = pt[3];
+        } else {
+            d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0u;
+        }
+        d.ep[0] = static_cast<uint32_t>(d6.v[0] | (d6.v[2] << 8) | (d6.v[4] << 16) | (d6.v[6] << 24));
+        d.ep[1] = static_cast<uint32_t>(d6.v[1] | (d6.v[3] << 8) | (d6.v[5] << 16) | (d6.v[7] << 24));
+        d.info = static_cast<uint32_t>(d6.parts - 1) | (1u << akv::kInfoReduced) |
+                 (static_cast<uint32_t>(wx) << akv::kInfoWx) | (static_cast<uint32_t>(wy) << akv::kInfoWy);
+        uint8_t codes[40];
+        for (int j = 0; j < 36; ++j) codes[j] = static_cast<uint8_t>(F::byte_of(d6.cw, j));
+        alignas(16) uint8_t w[72];
+        std::memset(w, 0xEE, sizeof(w));
+        for (int k = 0; k < 8 * wy; ++k)
+            if ((k & 7) < wx) w[k] = F::desc_weight(codes, 1, akv::g_akv_tables.wunq[d6.wq], wx, k);
+        constexpr int SEG = F::kDescSeg<6>;
+        for (int y = 0; y < 6; ++y)
+            for (int x0 = 0; x0 < 6; x0 += SEG) {
+                uint32_t c[SEG];
+                F::desc_seg_c16<6, SEG>(d.info, w, akv::row_pattern<6>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y),
+                                        d.ep[0], d.ep[1], y, x0, c);
+                for (int x = 0; x < SEG; ++x) o[y * 6 + x0 + x] = akv::c16_to_unit(c[x]);
+            }
+    }
+    return 0;
+}

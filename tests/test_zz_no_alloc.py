@@ -122,7 +122,7 @@ def test_noalloc_default_split_fits_the_static_array(cuda):
 def test_noalloc_rejects_scratch_beyond_its_maximum(cuda):
     from astc_kv_cuda import _lib as L
     lib = L.lib()
-    attn = _case()
+    attn, _ = _case()
     d = L.AkvAttnDesc.from_buffer_copy(attn.desc)
     # 4096 sequences x 9 heads x 8 splits x (64 + 2) floats > 8 MiB.
     d.batch = 4096
