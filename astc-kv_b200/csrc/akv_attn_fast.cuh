@@ -35,6 +35,8 @@
 #pragma once
 #include <math_constants.h>
 
+#include <type_traits>
+
 #include "akv_attention_kernels.cuh"
 #include "akv_common.cuh"
 #include "akv_decode_fast.cuh"
@@ -400,76 +402,6 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
         const int ncol = min(BS, D - col0);
         const float sc = affine ? __half2float(mscl[i]) : 0.f;
         const float of = affine ? __half2float(moff[i]) : 0.f;
-        if constexpr (BS == 6) {
-            // The table-driven header path: luminance blocks with a 6x6 grid
-            // (value table, then the texels) or a reduced grid (descriptor
-            // slot for phases 1a / 1b), and constant blocks.
-            const uint32_t f6 = __ldg(&g_f6.info[blk.x & 0x1FFFu]);
-            bool cst = (f6 & kF6Const) != 0, lum = false;
-            if (f6 & kF6Lum) {
-                const bool cem0 = (blk.x & 0x1800u) == 0 ? ((blk.x >> 13) & 15) == 0 : ((blk.x >> 23) & 0x3F) == 0;
-                if (cem0) {
-                    cst = (f6 & kF6Err) != 0;
-                    lum = !cst;
-                }
-            }
-            if (cst) {
-                ds.tab[0][tid] = table_entry(c16_to_unit(const_c16(blk)), affine, sc, of);
-                const uint32_t zero[9] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-                write6<LD>(zero, &ds.tab[0][tid], NC, norm, moff, mscl, row0, col0, thi, tlo);
-                continue;
-            }
-            if (lum) {
-                F6Lum o;
-                decode_f6_lum(blk, f6, &ds.codes[0][tid], NC, o);
-                if (f6 & kF6Full) {
-                    uint32_t idx[9];
-                    f6_entries(blk, o, idx);
-                    build_table(o.v, o.parts, o.wq, o.L, affine, sc, of, &ds.tab[0][tid], NC);
-                    write6<LD>(idx, &ds.tab[0][tid], NC, norm, moff, mscl, row0, col0, thi, tlo);
-                    continue;
-                }
-                // Reduced grid: a descriptor slot, its grid codes in this
-                // thread's code column for the late weight expansion.
-                const int slot = atomicAdd(&ds.nslot, 1);
-                if (slot >= kCap) {
-                    eval_block_generic<BS, LD>(blk, norm, sc, of, moff, mscl, row0, col0, rows, ncol, thi, tlo);
-                    continue;
-                }
-                const uint32_t me6 = __ldg(&g_akv_tables.mode[1][blk.x & 0x7FFu]);
-                const int wx = mode_wx(me6), wy = mode_wy(me6);
-                BlockDesc<1>& d = ds.desc[slot];
-                if (o.parts > 1) {
-                    const uint32_t* pt = g_akv_tables.part[1][o.parts - 2][(blk.x >> 13) & 0x3FF];
-                    d.pat[0] = __ldg(pt); d.pat[1] = __ldg(pt + 1);
-                    d.pat_hi[0] = __ldg(pt + 2); d.pat_hi[1] = __ldg(pt + 3);
-                } else {
-                    d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0u;
-                }
-                d.ep[0] = static_cast<uint32_t>(o.v[0] | (o.v[2] << 8) | (o.v[4] << 16) | (o.v[6] << 24));
-                d.ep[1] = static_cast<uint32_t>(o.v[1] | (o.v[3] << 8) | (o.v[5] << 16) | (o.v[7] << 24));
-                d.info = static_cast<uint32_t>(o.parts - 1) | (1u << kInfoReduced) |
-                         (static_cast<uint32_t>(wx) << kInfoWx) | (static_cast<uint32_t>(wy) << kInfoWy);
-                uint8_t* cc = &ds.codes[0][tid];
-                const int count = wx * wy;
-#pragma unroll
-                for (int j = 0; j < 36; ++j)
-                    if (j < count) cc[j * NC] = static_cast<uint8_t>(byte_of(o.cw, j));
-                ds.slot_pos[slot] = static_cast<uint32_t>(row0) | (static_cast<uint32_t>(col0) << 16) | kSlotRows;
-                ds.slot_aff[slot] = make_float2(sc, of);
-                if (late_w) {
-                    ds.slot_src[slot] = static_cast<uint32_t>(tid) | (static_cast<uint32_t>(o.wq) << 16);
-                } else {
-                    const uint8_t* un = g_akv_tables.wunq[o.wq];
-                    for (int r = 0; r < wy; ++r) {
-#pragma unroll
-                        for (int c = 0; c < BS; ++c)
-                            if (c < wx) ds.w[slot][8 * r + c] = desc_weight(cc, NC, un, wx, 8 * r + c);
-                    }
-                }
-                continue;
-            }
-        }
         uint32_t me;
         int cq;
         const int kind = block_kind<BS>(blk, me, cq);
@@ -707,7 +639,20 @@ __device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half
     __syncthreads();
 }
 
+}  // namespace fast
+}  // namespace akv
+
+#include "akv_decode6.cuh"
+
+namespace akv {
+namespace fast {
+
 // ------------------------------------------------------------------ kernel
+
+// Decode scratch of a plane of footprint BS with NB blocks per chunk: 6x6
+// planes take the sorted, class-specialised decode (akv_decode6.cuh).
+template <int NB, int NT, int BS>
+using PlaneScratch = std::conditional_t<BS == 6, Scratch6<NB>, DecodeScratch<NB, NT, BS>>;
 
 template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
 struct Cfg {
@@ -731,8 +676,8 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS>);
-    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
+    static constexpr size_t VDS = sizeof(PlaneScratch<VBLK, THREADS, VBS>);
+    static constexpr size_t KDS = KBS ? sizeof(PlaneScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
@@ -929,6 +874,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
                                                       CH / 4, n, valid, P,
                                                       *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, 4>*>(sm.ds),
                                                       sm.vhi, sm.vlo);
+        else if constexpr (VBS == 6)
+            decode_plane6<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
+                                                  CH / VBS, n, valid, *reinterpret_cast<Scratch6<C::VBLK>*>(sm.ds),
+                                                  sm.vhi, sm.vlo);
         else
             decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
                                                       C::VCOLS, CH / VBS, n, valid,
@@ -937,9 +886,15 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
-            decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
-                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS, KB>*>(sm.ds),
-                                                sm.khi, sm.klo);
+            if constexpr (KB == 6)
+                decode_plane6<D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
+                                                 CH / KB, n, valid, *reinterpret_cast<Scratch6<KN>*>(sm.ds), sm.khi,
+                                                 sm.klo);
+            else
+                decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
+                                                    CH / KB, n, valid,
+                                                    *reinterpret_cast<DecodeScratch<KN, THREADS, KB>*>(sm.ds), sm.khi,
+                                                    sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;
             if (sc > 0) {

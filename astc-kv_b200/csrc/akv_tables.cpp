@@ -328,6 +328,26 @@ void build_fast6_tables(const Tables& t, Fast6Tables* f) {
             }
         }
         f->info[v] = e;
+        // Header class (valid when every endpoint mode is 0; the kernel
+        // checks that and otherwise takes the runtime classifier).
+        uint8_t k = kC6Other;
+        if (e & kF6Const) {
+            k = kC6Const;
+        } else if (e & kF6Lum) {
+            if (e & kF6Err) {
+                k = kC6Const;  // error colour
+            } else if (!(e & kF6Full)) {
+                k = kC6Reduced;
+            } else {
+                for (int c = 0; c < kF6NumClasses; ++c)
+                    if (kF6Classes[c].wq == f6_wq(e) && kF6Classes[c].parts == f6_parts(e) &&
+                        kF6Classes[c].cq == f6_cq(e))
+                        k = static_cast<uint8_t>(kC6First + c);
+            }
+        }
+        // Bit 7: a luminance candidate (the class holds only with every
+        // endpoint mode 0).
+        f->klass[v] = static_cast<uint8_t>(k | ((e & kF6Lum) ? 0x80u : 0u));
     }
     for (int b = 0; b < 256; ++b)
         for (int j = 0; j < 4; ++j) f->spread2[b] |= static_cast<uint32_t>((b >> (2 * j)) & 3) << (8 * j);

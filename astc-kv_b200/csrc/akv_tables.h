@@ -90,8 +90,25 @@ AKV_HD constexpr int f6_wbits(uint32_t e) { return static_cast<int>((e >> 22) & 
 // (0..4), trits (0..2) and trits with one extra bit (0..5).
 enum : int { kF6W2 = 0, kF6W3 = 1, kF6Q0 = 2, kF6T0 = 3, kF6T1 = 4 };
 
+// Header classes of 6x6 blocks (Fast6Tables::klass): constant blocks, blocks
+// left to the runtime classifier, luminance blocks with a reduced grid, and
+// the luminance full-grid classes decoded by fully specialised code, each a
+// (weight range, partitions, colour range) triple. The colour range follows
+// from the other two (and the block mode) when every endpoint mode is 0.
+enum : int { kC6Const = 0, kC6Other = 1, kC6Reduced = 2, kC6First = 3 };
+struct F6Class {
+    int wq, parts, cq;
+};
+// Ordered by how often astcenc picks them for scalar KV data (the reference
+// corpus: 40 %, 26 %, 20 %, 5 % for the first four).
+constexpr F6Class kF6Classes[] = {{3, 2, 7},  {4, 1, 20}, {2, 3, 9},  {2, 2, 16}, {1, 4, 11},
+                                  {1, 3, 16}, {3, 1, 20}, {2, 1, 20}, {1, 1, 20}, {1, 2, 20}};
+constexpr int kF6NumClasses = static_cast<int>(sizeof(kF6Classes) / sizeof(kF6Classes[0]));
+constexpr int kC6Count = kC6First + kF6NumClasses;
+
 struct Fast6Tables {
     uint32_t info[8192];         // (mode | (partitions - 1) << 11) -> info entry, 0 = not on the fast path
+    uint8_t klass[8192];         // the same index -> header class (kC6*) | 0x80 for luminance candidates
     uint32_t spread2[256];       // four 2-bit fields -> four bytes
     uint32_t spread3[4096];      // four 3-bit fields -> four bytes
     uint32_t quint0[128];        // 7-bit quint block -> its three digits as bytes

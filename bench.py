@@ -737,6 +737,95 @@ def run_ours(args) -> dict | None:
     return line
 
 
+# ------------------------------------------------------- per-layer model step
+
+def run_c1_layers(args) -> dict | None:
+    """Config 1 as a model decode step issues it: one attention call per layer
+    (30 launches of split + merge, each timed with CUDA events), the same 30
+    calls replayed from one CUDA graph, and the single 30-layer launch, on the
+    same data. The reference never measured attention's share of a decode
+    step (docs/research_v4_report.md:85); this gives the per-layer figure."""
+    import torch
+    from astc_kv_cuda.ops import Attention, contiguous_astc_plane, contiguous_fp16_plane
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import astc_kv_cuda as A
+    A.init(local)
+    wl = Workload("c1", dev)
+    L, T, P = SPEC["c1"]["layers"], SPEC["c1"]["tokens"], 16
+    layers = []
+    for l in range(L):
+        kp = contiguous_fp16_plane(wl.kp.data[l:l + 1], P)
+        vp = contiguous_astc_plane(wl.vp.data[l:l + 1], wl.vp.offsets[l:l + 1], wl.vp.scales[l:l + 1], block=4,
+                                   layout="rgba", normalization="page_channel", head_dim=64, page_tokens=P)
+        layers.append(Attention(wl.q[l:l + 1], kp, vp, page_tokens=P, max_tokens=T, split_tokens=128))
+    stream = torch.cuda.current_stream()
+
+    def step_layers():
+        for a in layers:
+            a.run()
+
+    for _ in range(args.warmup):
+        step_layers()
+        wl.attn.run()
+    torch.cuda.synchronize()
+    # (1) per-layer launches with an event between layers.
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(L + 1)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            for l, a in enumerate(layers):
+                a.run()
+                evs[i][l + 1].record(stream)
+        torch.cuda.synchronize()
+    per_layer = [statistics.median(evs[i][l].elapsed_time(evs[i][l + 1]) for i in range(args.steps)) for l in range(L)]
+    step_ms = statistics.median(evs[i][0].elapsed_time(evs[i][L]) for i in range(args.steps))
+    # (2) the 30 calls as one CUDA graph.
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step_layers()
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step_layers()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    g1.record(stream)
+    torch.cuda.synchronize()
+    graph_ms = g0.elapsed_time(g1) / args.steps
+    # (3) the single 30-layer launch.
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        wl.attn.run()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    single_ms = s0.elapsed_time(s1) / args.steps
+    del graph
+    hbm, src = peaks()
+    tokens = L * T
+    return {"metric": METRIC + " [config 1 per-layer decode step]", "value": tokens / (graph_ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": graph_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded per unit)",
+            "config": {**line_config("c1", 1, "replica"), "step": "30 attention calls (one per layer), CUDA graph"},
+            "per_layer": {"layer_us_median": [round(x * 1e3, 2) for x in per_layer],
+                          "layer_us_mean": sum(per_layer) / L * 1e3,
+                          "eager_30_launches_ms": step_ms, "graph_30_launches_ms": graph_ms,
+                          "single_30_layer_launch_ms": single_ms,
+                          "roofline_frac_graph": job_bytes("c1") / (graph_ms * 1e-3) / 1e9 / hbm,
+                          "roofline_frac_single": job_bytes("c1") / (single_ms * 1e-3) / 1e9 / hbm},
+            "clocks": clk.summary(), "gpu_launches": 2 * L * args.steps}
+
+
 # ----------------------------------------------------------------- decode bench
 
 class DecodeWorkload:
@@ -928,6 +1017,9 @@ def main():
     ap.add_argument("--decode-blocks", type=int, default=1 << 26,
                     help="blocks per step of the decode microbench (a multiple of 2^20; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-layer", action="store_true",
+                    help="c1 only: time one attention call per layer (eager and as one CUDA graph) next to the "
+                         "single 30-layer launch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -935,6 +1027,10 @@ def main():
         line = run_reference(args)
     elif args.workload.startswith("decode"):
         line = run_decode(args)
+    elif args.per_layer:
+        if args.workload != "c1":
+            raise SystemExit("--per-layer is for the c1 workload")
+        line = run_c1_layers(args)
     else:
         line = run_ours(args)
     if line is not None:

@@ -43,6 +43,7 @@ inline float __uint_as_float(unsigned int i) { float f; std::memcpy(&f, &i, 4); 
 inline unsigned int __float_as_uint(float f) { unsigned int i; std::memcpy(&i, &f, 4); return i; }
 #include "../../astc-kv_b200/csrc/akv_astc_device.cuh"
 #include "../../astc-kv_b200/csrc/akv_decode_fast.cuh"
+#include "../../astc-kv_b200/csrc/akv_decode6.cuh"
 
 extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, uint16_t* out) {
     static bool ready = false;
@@ -229,13 +230,13 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
     return 0;
 }
 
-// The attention kernel's 6x6 table-driven header path (decode_plane's block
-// phase for 6x6 planes): constant blocks, luminance blocks with a full grid
-// (value table of unit values + per-texel entry bytes, read back as write6
-// reads them) or a reduced grid (descriptor, then desc_seg_c16 as phase 1b
-// evaluates it); anything else takes the runtime path (fast_r_one).
-// cls: 10 constant, 11 full-grid table, 12 reduced-grid descriptor, else the
-// runtime path's kind.
+// The attention kernel's 6x6 decode (akv_decode6.cuh), block by block as its
+// header phase handles them: the class lookup, then constant blocks,
+// specialised luminance classes (value table of unit values + per-texel entry
+// bytes, read back as the texel phase reads them), reduced grids (table
+// header decode, descriptor, then desc_seg_c16 as phase 1b evaluates it) and
+// everything else through the runtime path (fast_r_one).
+// cls: 100 + header class for the class paths, else the runtime path's kind.
 extern "C" int emu_decode_f6(const uint8_t* blocks, int64_t n, float* out, int* cls) {
     static bool ready = false;
     if (!ready) {
@@ -248,45 +249,42 @@ extern "C" int emu_decode_f6(const uint8_t* blocks, int64_t n, float* out, int* 
         uint4 blk;
         std::memcpy(&blk, blocks + 16 * i, 16);
         float* o = out + i * 36;
-        const uint32_t f6 = F::g_f6.info[blk.x & 0x1FFFu];
-        bool cst = (f6 & akv::kF6Const) != 0, lum = false;
-        if (f6 & akv::kF6Lum) {
+        int k = F::g_f6.klass[blk.x & 0x1FFFu];
+        if (k & 0x80) {
             const bool cem0 = (blk.x & 0x1800u) == 0 ? ((blk.x >> 13) & 15) == 0 : ((blk.x >> 23) & 0x3F) == 0;
-            if (cem0) {
-                cst = (f6 & akv::kF6Err) != 0;
-                lum = !cst;
-            }
+            k = cem0 ? (k & 0x7F) : akv::kC6Other;
         }
-        if (cst) {
-            cls[i] = 10;
-            const float u = akv::c16_to_unit(F::const_c16(blk));
-            for (int t = 0; t < 36; ++t) o[t] = u;
-            continue;
-        }
-        if (!lum) {
+        if (k == akv::kC6Other) {
             const int rc = fast_r_one<6>(blk, cls + i, o);
             if (rc) return rc;
             continue;
         }
-        uint8_t cscr[40];
-        std::memset(cscr, 0xEE, sizeof(cscr));
-        F::F6Lum d6;
-        F::decode_f6_lum(blk, f6, cscr, 1, d6);
-        if (f6 & akv::kF6Full) {
-            cls[i] = 11;
-            uint32_t idx[9];
-            F::f6_entries(blk, d6, idx);
-            uint32_t tab[F::kTabCapMax];
+        cls[i] = 100 + k;
+        if (k == akv::kC6Const) {
+            const float u = akv::c16_to_unit(F::const_c16(blk));
+            for (int t = 0; t < 36; ++t) o[t] = u;
+            continue;
+        }
+        if (k >= akv::kC6First) {
+            uint32_t tab[12];
             std::memset(tab, 0xEE, sizeof(tab));
-            F::build_table(d6.v, d6.parts, d6.wq, d6.L, false, 0.f, 0.f, tab, 1);
+            uint32_t idx[9];
+            F::decode_class6_any(k - akv::kC6First, blk, false, 0.f, 0.f, tab, 1, idx,
+                                 std::make_integer_sequence<int, akv::kF6NumClasses>{});
+            const akv::F6Class c = akv::kF6Classes[k - akv::kC6First];
+            const int L = F::kLevelsCt[c.wq];
             for (int t = 0; t < 36; ++t) {
                 const uint32_t e = F::byte_of(idx, t);
-                if (e >= static_cast<uint32_t>(d6.parts * d6.L)) return 4;
+                if (e >= static_cast<uint32_t>(c.parts * L)) return 4;
                 o[t] = __uint_as_float(tab[e]);
             }
             continue;
         }
-        cls[i] = 12;
+        // Reduced grid through the table header decode and a descriptor.
+        uint8_t cscr[40];
+        std::memset(cscr, 0xEE, sizeof(cscr));
+        F::F6Lum d6;
+        F::decode_f6_lum(blk, F::g_f6.info[blk.x & 0x1FFFu], cscr, 1, d6);
         const uint32_t me = akv::g_akv_tables.mode[1][blk.x & 0x7FFu];
         const int wx = akv::mode_wx(me), wy = akv::mode_wy(me);
         akv::BlockDesc<1> d;
@@ -304,8 +302,8 @@ extern "C" int emu_decode_f6(const uint8_t* blocks, int64_t n, float* out, int* 
         for (int j = 0; j < 36; ++j) codes[j] = static_cast<uint8_t>(F::byte_of(d6.cw, j));
         alignas(16) uint8_t w[72];
         std::memset(w, 0xEE, sizeof(w));
-        for (int k = 0; k < 8 * wy; ++k)
-            if ((k & 7) < wx) w[k] = F::desc_weight(codes, 1, akv::g_akv_tables.wunq[d6.wq], wx, k);
+        for (int q = 0; q < 8 * wy; ++q)
+            if ((q & 7) < wx) w[q] = F::desc_weight(codes, 1, akv::g_akv_tables.wunq[d6.wq], wx, q);
         constexpr int SEG = F::kDescSeg<6>;
         for (int y = 0; y < 6; ++y)
             for (int x0 = 0; x0 < 6; x0 += SEG) {

@@ -144,12 +144,13 @@ def test_rgba4_fast_decode_matches_oracle(source):
 
 
 @pytest.mark.parametrize("source", ["golden", "story", "random", "garbage", "encoder"])
-def test_f6_table_header_path_matches_oracle(source):
-    """The 6x6 table-driven header path of the attention kernel (block-mode
-    info lookup, weight groups decoded by window lookups into code bytes,
-    per-texel entry bytes from codes + L * partition; reduced grids through
-    the descriptor evaluator) against the oracle's fp16 view, bit for bit.
-    The reference's astcenc blocks must nearly all take the table path."""
+def test_f6_class_decode_matches_oracle(source):
+    """The attention kernel's 6x6 decode (class lookup; specialised classes
+    with colour and weight groups at compile-time positions, weight groups by
+    window lookups into code bytes, per-texel entry bytes from codes + L *
+    partition; reduced grids through the descriptor evaluator; the runtime
+    path for the rest) against the oracle's fp16 view, bit for bit. The
+    reference's astcenc blocks must nearly all take the class paths."""
     from astc_kv_cuda.ops import host_encode, random_blocks
     if source == "golden":
         blocks = golden("block_geometry_identity")["blocks"].reshape(-1, 16)
@@ -174,6 +175,6 @@ def test_f6_table_header_path_matches_oracle(source):
     np.testing.assert_array_equal(got, ref)
     if source in ("golden", "story"):
         # A few astcenc blocks use wider weight ranges (0..9 and up) and take
-        # the runtime path; the rest take the table-driven one.
-        fast = np.isin(cls, (10, 11, 12)).mean()
-        assert (cls == 11).mean() > 0.9 and fast > 0.99, np.unique(cls, return_counts=True)
+        # the runtime path; the rest take the class paths (100 + class:
+        # 100 constant, 102 reduced grid, 103.. the specialised full grids).
+        assert (cls >= 103).mean() > 0.9 and (cls >= 100).mean() > 0.99, np.unique(cls, return_counts=True)
