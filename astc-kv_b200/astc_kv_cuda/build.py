@@ -21,7 +21,7 @@ LIB = PKG / "libakv_cuda.so"
 
 SOURCES = ["akv_cuda.cu", "akv_tables.cpp", "akv_encode.cpp"]
 HEADERS = ["akv_astc_device.cuh", "akv_common.cuh", "akv_decode_kernels.cuh", "akv_attention_kernels.cuh", "akv_tables.h",
-           "akv_attn_fp16.cuh", "akv_decode6.cuh",
+           "akv_attn_fp16.cuh",
            "akv_attn_fast.cuh", "akv_decode_fast.cuh"]
 
 

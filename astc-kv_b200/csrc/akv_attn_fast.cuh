@@ -20,11 +20,11 @@
 //   * Tensor cores (mma.sync m16n8k16, fp32 accumulation). Every warp owns
 //     one (16-token tile, half of the head dims) pair; the query heads of
 //     the GQA group are the N=8 dimension:
-//       S^T[tok][head] = K . Q^T   (q hi+lo; K fp16 straight from global
-//                                   memory in fragment order (L2-prefetched
-//                                   a chunk ahead), or decoded K hi+lo from
-//                                   shared memory; both warps of a tile
-//                                   compute it)
+//       S^T[tok][head] = K . Q^T   (q hi+lo; FP16 K staged in shared memory
+//                                   by 16-byte cp.async copies issued a
+//                                   chunk ahead (they land during the
+//                                   chunk's decode), or decoded K hi+lo;
+//                                   both warps of a tile compute it)
 //       online softmax per head in base 2, P^T as fp16 through a 256-byte
 //       per-warp buffer,
 //       O^T[dim][head] += V^T . P^T  for the warp's dim half (V hi and lo,
@@ -34,8 +34,6 @@
 //     acc), the same workspace format the merge kernel reads.
 #pragma once
 #include <math_constants.h>
-
-#include <type_traits>
 
 #include "akv_attention_kernels.cuh"
 #include "akv_common.cuh"
@@ -93,6 +91,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+
+// 16-byte global -> shared asynchronous copy; `bytes` 0 writes zeros (the
+// source is then not read).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // L2 prefetch of one global-memory line.
 __device__ __forceinline__ void prefetch_l2(const void* ptr) {
@@ -185,8 +192,10 @@ template <int NB, int NT, int BS>
 struct DecodeScratch {
     static constexpr int N = BS * BS;
     // Descriptor slots: every block of a small chunk (8x8 planes are mostly
-    // reduced grids), at most 64.
-    static constexpr int kSlowCap = NB < 64 ? NB : 64;
+    // reduced grids), at most 64; 40 for 6x6 planes (astcenc's 6x6 chunks
+    // hold about ten descriptor blocks in 176).
+    static constexpr int kSlowMax = BS == 6 ? 40 : 64;
+    static constexpr int kSlowCap = NB < kSlowMax ? NB : kSlowMax;
     // Columns: one per decoding thread (a chunk with fewer blocks than
     // threads leaves the others idle).
     static constexpr int NC = NT < ((NB + 31) / 32) * 32 ? NT : ((NB + 31) / 32) * 32;
@@ -639,20 +648,7 @@ __device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half
     __syncthreads();
 }
 
-}  // namespace fast
-}  // namespace akv
-
-#include "akv_decode6.cuh"
-
-namespace akv {
-namespace fast {
-
 // ------------------------------------------------------------------ kernel
-
-// Decode scratch of a plane of footprint BS with NB blocks per chunk: 6x6
-// planes take the sorted, class-specialised decode (akv_decode6.cuh).
-template <int NB, int NT, int BS>
-using PlaneScratch = std::conditional_t<BS == 6, Scratch6<NB>, DecodeScratch<NB, NT, BS>>;
 
 template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
 struct Cfg {
@@ -676,13 +672,13 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    static constexpr size_t VDS = sizeof(PlaneScratch<VBLK, THREADS, VBS>);
-    static constexpr size_t KDS = KBS ? sizeof(PlaneScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
+    static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS>);
+    static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
     static_assert(CH % VBS == 0 && CH % (KBS ? KBS : 1) == 0, "chunk must hold whole block rows");
     static_assert(G <= 8, "query group must fit the N=8 MMA dimension");
     // Overhanging block columns stay inside the tile rows and metadata.
-    static_assert((D + VBS - 1) / VBS * VBS <= LD && (!KBS || (D + KBS - 1) / KBS * KBS <= LD), "tile row padding");
+    static_assert((D + VBS - 1) / VBS * VBS <= LD && (!KBS || (D + MAXBS - 1) / MAXBS * MAXBS <= LD), "tile row padding");
     static_assert(VL == AKV_LAYOUT_RGBA || (D + VBS - 1) / VBS * VBS <= META, "metadata padding");
     static_assert(VL == AKV_LAYOUT_SCALAR || (VBS == 4 && KBS == 0 && D % 16 == 0), "RGBA: 4x4 V, FP16 K");
 };
@@ -699,7 +695,7 @@ struct Smem {
     __align__(16) __half kside[2][KBS ? C::SIDE : 1];
     __align__(16) __half vhi[C::CH][C::LD];
     __align__(16) __half vlo[C::CH][C::LD];
-    __align__(16) __half khi[KBS ? C::CH : 1][C::LD];
+    __align__(16) __half khi[C::CH][C::LD];   // decoded K hi, or the staged FP16 K rows
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[2 * C::NWM][8][16];
@@ -819,11 +815,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         const int64_t qb = (static_cast<int64_t>(b) * p.Hq + h * G + (has ? qn : 0)) * D;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-            // Natural dim order for decoded K; a permuted order for direct
-            // FP16 K loads (see the K loader below).
-            int d0, d1;
-            if (KBS > 0) { d0 = 16 * ks + 2 * qj; d1 = d0 + 8; }
-            else { const int g32 = ks >> 1, half = ks & 1; d0 = 32 * g32 + 8 * qj + 4 * half; d1 = d0 + 2; }
+            const int d0 = 16 * ks + 2 * qj, d1 = d0 + 8;
             const float q0 = has ? load_q(p.q, p.q_dtype, qb + d0) : 0.f;
             const float q1 = has ? load_q(p.q, p.q_dtype, qb + d0 + 1) : 0.f;
             const float q2 = has ? load_q(p.q, p.q_dtype, qb + d1) : 0.f;
@@ -835,20 +827,26 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         }
     }
 
-    auto prefetch_k = [&](int c) {
+    // FP16 K rows of chunk c -> sm.khi by 16-byte asynchronous copies (rows
+    // past the split or on unmapped pages copy zero bytes: zeros).
+    auto stage_k = [&](int c) {
         if constexpr (KBS == 0) {
-            if (dh == 0 && c < nchunks) {
-                const int tt = t_begin + c * CH + 16 * tw + (lane >> 1);
-                if (tt < t_end && (lane & 1) * 128 < D * 2) {
-                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
-                    if (phys >= 0)
-                        prefetch_l2(p.k.data + b * p.k.sB + h * p.k.sH + static_cast<int64_t>(phys) * p.k.sP +
-                                    static_cast<int64_t>(tt % P) * D * 2 + (lane & 1) * 128);
-                }
+            constexpr int PPR = D / 8, PIECES = CH * PPR;
+            const int t0 = t_begin + c * CH;
+            const uint8_t* kbase = p.k.data + b * p.k.sB + h * p.k.sH;
+            for (int piece = tid; piece < PIECES; piece += THREADS) {
+                const int r = piece / PPR, j = piece - r * PPR;
+                const int t = t0 + r;
+                const int phys = t < t_end ? phys_page(p.table, p.pps, p.num_pages, b, t / P, nullptr) : -1;
+                const uint8_t* src =
+                    phys >= 0 ? kbase + static_cast<int64_t>(phys) * p.k.sP + static_cast<int64_t>(t % P) * (D * 2) + j * 16
+                              : kbase;
+                cp_async16(&sm.khi[r][8 * j], src, phys >= 0 ? 16u : 0u);
             }
+            cp_async_commit();
         }
     };
-    prefetch_k(0);
+    stage_k(0);
 
     float o[KH][4];
 #pragma unroll
@@ -867,17 +865,12 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
             break;
         }
         const bool valid = sm.valid[s] != 0;
-        prefetch_k(c + 1);
         // Decode V (and K) tiles.
         if constexpr (VL == AKV_LAYOUT_RGBA)
             decode_plane_rgba<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
                                                       CH / 4, n, valid, P,
                                                       *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, 4>*>(sm.ds),
                                                       sm.vhi, sm.vlo);
-        else if constexpr (VBS == 6)
-            decode_plane6<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
-                                                  CH / VBS, n, valid, *reinterpret_cast<Scratch6<C::VBLK>*>(sm.ds),
-                                                  sm.vhi, sm.vlo);
         else
             decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
                                                       C::VCOLS, CH / VBS, n, valid,
@@ -886,15 +879,9 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
-            if constexpr (KB == 6)
-                decode_plane6<D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
-                                                 CH / KB, n, valid, *reinterpret_cast<Scratch6<KN>*>(sm.ds), sm.khi,
-                                                 sm.klo);
-            else
-                decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
-                                                    CH / KB, n, valid,
-                                                    *reinterpret_cast<DecodeScratch<KN, THREADS, KB>*>(sm.ds), sm.khi,
-                                                    sm.klo);
+            decode_plane<KB, D, THREADS, KN, LD>(sm.kraw[s], sm.kmeta[s][0], sm.kmeta[s][1], p.k.norm, C::KCOLS,
+                                                CH / KB, n, valid, *reinterpret_cast<DecodeScratch<KN, THREADS, KB>*>(sm.ds),
+                                                sm.khi, sm.klo);
             // Exact side-plane channels.
             const int sc = p.k.side_count;
             if (sc > 0) {
@@ -928,30 +915,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
             }
             __syncthreads();
         }
-        // Direct FP16 K fragments for this warp's 16 tokens (loaded after the
-        // decode so they do not hold registers through it). Permuted dims:
-        // lane quad j of row r loads dims [32g + 8j, 32g + 8j + 8) for each
-        // 32-dim group g.
-        uint4 kreg[KBS ? 1 : D / 32][2];
         if constexpr (KBS == 0) {
-            {
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    const int tr = 16 * tw + qn + 8 * rr;
-                    const int tt = t0 + tr;
-                    const uint4* row = nullptr;
-                    if (tr < n) {
-                        const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
-                        if (phys >= 0)
-                            row = reinterpret_cast<const uint4*>(p.k.data + b * p.k.sB + h * p.k.sH +
-                                                                 static_cast<int64_t>(phys) * p.k.sP +
-                                                                 static_cast<int64_t>(tt % P) * D * 2);
-                    }
-#pragma unroll
-                    for (int g32 = 0; g32 < D / 32; ++g32)
-                        kreg[g32][rr] = row ? __ldg(row + 4 * g32 + qj) : make_uint4(0, 0, 0, 0);
-                }
-            }
+            // This chunk's K rows have landed (issued a chunk ahead).
+            cp_async_wait<0>();
+            __syncthreads();
         }
         // The raw stage is consumed: refill it with chunk c + 2.
         if (tid == 0 && c + 2 < nchunks) {
@@ -969,22 +936,15 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
                 const uint4 qf = sm.qfrag[ks][lane];
                 float* acc = sa[ks & 1];
                 uint32_t a[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
+                const int col = 16 * ks + ((mi & 2) ? 8 : 0);
+                ldsm_x4(a, &sm.khi[row][col]);
+                mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
                 if constexpr (KBS > 0) {
-                    const int mi = lane >> 3, rr = lane & 7;
-                    const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
-                    const int col = 16 * ks + ((mi & 2) ? 8 : 0);
-                    ldsm_x4(a, &sm.khi[row][col]);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
                     ldsm_x4(a, &sm.klo[row][col]);
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                } else {
-                    const uint4 r0 = kreg[ks >> 1][0];
-                    const uint4 r1 = kreg[ks >> 1][1];
-                    if ((ks & 1) == 0) { a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y; }
-                    else { a[0] = r0.z; a[2] = r0.w; a[1] = r1.z; a[3] = r1.w; }
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
                 }
             }
             float sacc[4];
@@ -1050,7 +1010,9 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
             __syncwarp();
         }
         __syncthreads();  // tiles and P buffers free for the next chunk
+        if (c + 1 < nchunks) stage_k(c + 1);
     }
+    if constexpr (KBS == 0) cp_async_wait<0>();  // nothing in flight past the loop
 
     if (stuck >= 0) {
         // A copy never completed: report, give the copies still in flight

@@ -29,20 +29,13 @@
 namespace akv {
 namespace f16k {
 
+using fast::cp_async16;
+using fast::cp_async_commit;
+using fast::cp_async_wait;
 using fast::ldsm_x4;
 using fast::ldsm_x4_t;
 using fast::mma16816;
-using fast::smem_u32;
 using fast::split_pair;
-
-// 16-byte global -> shared asynchronous copy; `bytes` 0 writes zeros (the
-// source is then not read).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int D, int G>
 struct Cfg {

@@ -33,15 +33,12 @@ std::mutex g_init_mu;
 // so a caller that resets a device must not use this library on it again.
 std::atomic<bool> g_init_done[kMaxDevices];
 Tables* g_host_tables = nullptr;
-Fast6Tables* g_host_f6 = nullptr;
 
 const Tables& host_tables() {
     static std::once_flag once;
     std::call_once(once, [] {
         g_host_tables = new Tables;
         build_tables(g_host_tables);
-        g_host_f6 = new Fast6Tables;
-        build_fast6_tables(*g_host_tables, g_host_f6);
     });
     return *g_host_tables;
 }
@@ -55,7 +52,6 @@ int init_device(int device) {
     if (prev != device && cudaSetDevice(device) != cudaSuccess) return AKV_ERR_CUDA;
     const Tables& t = host_tables();
     cudaError_t e = cudaMemcpyToSymbol(g_akv_tables, &t, sizeof(Tables), 0, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(fast::g_f6, g_host_f6, sizeof(Fast6Tables), 0, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (prev != device) cudaSetDevice(prev);
     if (e != cudaSuccess) return AKV_ERR_CUDA;

@@ -15,17 +15,10 @@
 #pragma once
 #include <cuda_fp16.h>
 
-#include <utility>
-
-#include "../../include/akv_cuda.h"
 #include "akv_astc_device.cuh"
 
 namespace akv {
 namespace fast {
-
-// Tables of the 6x6 fast header path (akv_tables.h), filled per device by
-// akv_cuda_init next to g_akv_tables.
-__device__ Fast6Tables g_f6;
 
 
 // Block kinds of the runtime path.
@@ -39,10 +32,13 @@ constexpr bool kDirect = BS == 4;
 
 // Value-table capacity per block (entries = partitions * weight levels) by
 // footprint: none for directly evaluated 4x4 blocks; a full-resolution 8x8
-// grid only fits two weight levels (at most 8 entries).
+// grid only fits two weight levels (at most 8 entries); 12 for 6x6, the
+// largest table of any full-grid block in the reference's astcenc corpus
+// (three partitions x four levels, four x three), larger ones become
+// descriptors.
 template <int BS>
-constexpr int kTabCap = BS == 4 ? 0 : (BS == 8 ? 8 : 24);
-constexpr int kTabCapMax = 24;
+constexpr int kTabCap = BS == 4 ? 0 : (BS == 8 ? 8 : 12);
+constexpr int kTabCapMax = 12;
 
 __device__ __forceinline__ int range_levels(int q) {
     const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
@@ -376,175 +372,6 @@ __device__ __forceinline__ float lum_unit(const LumOut& o, const uint32_t* tab, 
     const uint32_t c = codes[t * nt] & o.cmask;
     const uint32_t part = (o.pat[t >> 4] >> (2 * (t & 15))) & 3u;
     return __uint_as_float(tab[(part * o.L + c) * nt]);
-}
-
-// ------------------------------------------------------ 6x6 fast headers
-//
-// A 6x6 block whose 13 low bits (block mode, partition count) the info table
-// marks as a luminance candidate, and whose endpoint modes are all 0, is
-// decoded without any runtime bit-stream loop: the colour integers by the
-// runtime BISE step loop (one or two steps), every weight group by one lookup
-// of its whole bit window at a compile-time position of the bit-reversed
-// weight stream, giving packed code bytes. For a full 6x6 grid the code bytes
-// plus L times the partition index (bytes from the partition pattern) give
-// each texel's value-table entry, four texels per add.
-
-// Bits [POS, POS + N) of the 128-bit value w (w[0] = bits 0..31), N <= 25.
-template <int POS, int N>
-__device__ __forceinline__ uint32_t bits128(const uint32_t (&w)[4]) {
-    constexpr int k = POS >> 5, sh = POS & 31;
-    uint32_t v;
-    if constexpr (k >= 4) v = 0u;
-    else if constexpr (sh + N <= 32 || k == 3) v = w[k] >> sh;
-    else v = __funnelshift_r(w[k], w[k + 1], sh);
-    return v & ((1u << N) - 1u);
-}
-
-// OR an NB-byte value (lo: bytes 0..3, hi: byte 4) into byte offset O of the
-// 36 code bytes cw (bytes past 35 are dropped).
-template <int O, int NB>
-__device__ __forceinline__ void place_bytes(uint32_t (&cw)[9], uint32_t lo, uint32_t hi) {
-    constexpr int k = O >> 2, sh = 8 * (O & 3);
-    if constexpr (k < 9) cw[k] |= lo << sh;
-    if constexpr (k + 1 < 9) {
-        if constexpr (sh > 0 && (O & 3) + (NB < 4 ? NB : 4) > 4) cw[k + 1] |= lo >> (32 - sh);
-        if constexpr (NB == 5) cw[k + 1] |= hi << sh;
-    }
-}
-
-// Group G of a weight stream of kind KIND -> its code bytes in cw.
-template <int KIND, int G>
-__device__ __forceinline__ void weight_group6(const uint32_t (&w)[4], uint32_t (&cw)[9]) {
-    const Fast6Tables& F = g_f6;
-    if constexpr (KIND == kF6W2) {          // stream byte G = codes 4G..4G+3
-        cw[G] = __ldg(&F.spread2[bits128<8 * G, 8>(w)]);
-    } else if constexpr (KIND == kF6W3) {   // 12 bits = codes 4G..4G+3
-        cw[G] = __ldg(&F.spread3[bits128<12 * G, 12>(w)]);
-    } else if constexpr (KIND == kF6Q0) {   // 7-bit quint block = codes 3G..3G+2
-        place_bytes<3 * G, 3>(cw, __ldg(&F.quint0[bits128<7 * G, 7>(w)]), 0u);
-    } else {                                // 8-bit trit block / 13-bit trit+bit group = codes 5G..5G+4
-        constexpr int GB = KIND == kF6T0 ? 8 : 13;
-        const uint32_t* e = KIND == kF6T0 ? F.trit0[bits128<GB * G, GB>(w)] : F.trit1[bits128<GB * G, GB>(w)];
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(e));
-        place_bytes<5 * G, 5>(cw, v.x, v.y);
-    }
-}
-
-template <int KIND, int... G>
-__device__ __forceinline__ void weight_groups6(const uint32_t (&w)[4], uint32_t (&cw)[9],
-                                               std::integer_sequence<int, G...>) {
-    (weight_group6<KIND, G>(w, cw), ...);
-}
-
-// All 36 code bytes (fewer for a reduced grid; the rest are don't-care) of a
-// weight stream of kind KIND; w is the bit-reversed block masked to the
-// stream's length.
-template <int KIND>
-__device__ __forceinline__ void weight_codes6(const uint32_t (&w)[4], uint32_t (&cw)[9]) {
-#pragma unroll
-    for (int k = 0; k < 9; ++k) cw[k] = 0u;
-    constexpr int NG = KIND == kF6Q0 ? 12 : (KIND == kF6W2 || KIND == kF6W3) ? 9 : 8;
-    weight_groups6<KIND>(w, cw, std::make_integer_sequence<int, NG>{});
-}
-
-// Byte i of the 36-byte array held in 9 words.
-__device__ __forceinline__ uint32_t byte_of(const uint32_t (&a)[9], int i) {
-    return (a[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-}
-
-// What the 6x6 fast path decodes from a luminance block (endpoint modes 0).
-struct F6Lum {
-    int v[8];          // colour integers (unquantised), 2 per partition
-    uint32_t cw[9];    // weight codes as bytes, in stream order
-    int parts, wq, L;
-};
-
-__device__ __forceinline__ void decode_f6_lum(uint4 blk, uint32_t info, uint8_t* cscr, int nt, F6Lum& o) {
-    const uint64_t lo = (static_cast<uint64_t>(blk.y) << 32) | blk.x;
-    const uint64_t hi = (static_cast<uint64_t>(blk.w) << 32) | blk.z;
-    o.parts = f6_parts(info);
-    o.wq = f6_wq(info);
-    o.L = f6_levels(info);
-    const int cq = f6_cq(info);
-    {
-        // Colour integers through the thread's scratch column, read back.
-        const int cstart = o.parts == 1 ? 17 : 29;
-        uint64_t clo = window_u128(lo, hi, cstart);
-        uint64_t chi = hi >> cstart;
-        mask_u128(clo, chi, bise_stream_bits_dev(2 * o.parts, cq));
-        color_values(clo, chi, cq, 2 * o.parts, cscr, nt);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) o.v[k] = cscr[k * nt];
-    }
-    uint64_t s0 = __brevll(hi), s1 = __brevll(lo);
-    mask_u128(s0, s1, f6_wbits(info));
-    const uint32_t w[4] = {static_cast<uint32_t>(s0), static_cast<uint32_t>(s0 >> 32), static_cast<uint32_t>(s1),
-                           static_cast<uint32_t>(s1 >> 32)};
-    switch (f6_kind(info)) {
-        case kF6W2: weight_codes6<kF6W2>(w, o.cw); break;
-        case kF6W3: weight_codes6<kF6W3>(w, o.cw); break;
-        case kF6Q0: weight_codes6<kF6Q0>(w, o.cw); break;
-        case kF6T0: weight_codes6<kF6T0>(w, o.cw); break;
-        default: weight_codes6<kF6T1>(w, o.cw); break;
-    }
-}
-
-// Value-table entries of texels 0..35 as bytes: code + L * partition.
-__device__ __forceinline__ void f6_entries(uint4 blk, const F6Lum& o, uint32_t (&idx)[9]) {
-    if (o.parts > 1) {
-        const uint32_t* pt = g_akv_tables.part[1][o.parts - 2][(blk.x >> 13) & 0x3FF];
-        const uint32_t pw[3] = {__ldg(pt), __ldg(pt + 1), __ldg(pt + 2)};
-        const uint32_t L = static_cast<uint32_t>(o.L);
-#pragma unroll
-        for (int k = 0; k < 9; ++k)
-            idx[k] = o.cw[k] + L * __ldg(&g_f6.spread2[(pw[k >> 2] >> (8 * (k & 3))) & 0xFFu]);
-    } else {
-#pragma unroll
-        for (int k = 0; k < 9; ++k) idx[k] = o.cw[k];
-    }
-}
-
-// The 36 texels of a 6x6 table / constant block from their entry bytes ->
-// the hi/lo tiles (pairs of columns per 32-bit store). As write_block: a
-// block overhanging the head dimension writes its extra columns into the
-// tile rows' padding; rows past the chunk's tokens are zeroed afterwards.
-template <int LD>
-__device__ __forceinline__ void write6(const uint32_t (&idx)[9], const uint32_t* tab, int nt, int norm,
-                                       const __half* moff, const __half* mscl, int row0, int col0,
-                                       __half (*thi)[LD], __half (*tlo)[LD]) {
-    const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
-#pragma unroll
-    for (int y = 0; y < 6; ++y) {
-        float rs = 0.f, ro = 0.f;
-        if (norm == AKV_NORM_TOKEN) {
-            rs = __half2float(mscl[row0 + y]);
-            ro = __half2float(moff[row0 + y]);
-        }
-#pragma unroll
-        for (int x = 0; x < 6; x += 2) {
-            const int i = 6 * y + x;
-            const uint32_t a = tab[byte_of(idx, i) * nt], b2 = tab[byte_of(idx, i + 1) * nt];
-            uint32_t h, l;
-            if (affine) {
-                h = __byte_perm(a, b2, 0x5410);
-                l = __byte_perm(a, b2, 0x7632);
-            } else {
-                float s0 = rs, o0 = ro, s1 = rs, o1 = ro;
-                if (norm == AKV_NORM_PAGE_CHANNEL) {
-                    s0 = __half2float(mscl[col0 + x]); o0 = __half2float(moff[col0 + x]);
-                    s1 = __half2float(mscl[col0 + x + 1]); o1 = __half2float(moff[col0 + x + 1]);
-                }
-                const float va = fmaf(__uint_as_float(a), s0, o0), vb = fmaf(__uint_as_float(b2), s1, o1);
-                const __half2 hh = __floats2half2_rn(va, vb);
-                const float2 hf = __half22float2(hh);
-                const __half2 ll = __floats2half2_rn(va - hf.x, vb - hf.y);
-                h = *reinterpret_cast<const uint32_t*>(&hh);
-                l = *reinterpret_cast<const uint32_t*>(&ll);
-            }
-            *reinterpret_cast<uint32_t*>(&thi[row0 + y][col0 + x]) = h;
-            *reinterpret_cast<uint32_t*>(&tlo[row0 + y][col0 + x]) = l;
-        }
-    }
 }
 
 // ------------------------------------------------- RGBA layout, 4x4 blocks

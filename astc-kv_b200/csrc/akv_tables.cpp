@@ -300,83 +300,4 @@ void build_tables(Tables* t) {
     }
 }
 
-void build_fast6_tables(const Tables& t, Fast6Tables* f) {
-    std::memset(f, 0, sizeof(*f));
-    const int fp = 1;  // 6x6
-    for (int v = 0; v < 8192; ++v) {
-        const int mode = v & 0x7FF, parts = ((v >> 11) & 3) + 1;
-        uint32_t e = 0;
-        if ((mode & 0x1FF) == 0x1FC) {
-            e = kF6Const;  // void extent (its own checks decide the colour)
-        } else {
-            const uint32_t me = t.mode[fp][mode];
-            if (!(me & kModeValid)) {
-                e = kF6Const;  // reserved mode: error colour
-            } else if (!(me & kModeDual)) {
-                const int wq = mode_wq(me), wx = mode_wx(me), wy = mode_wy(me), wbits = mode_wbits(me);
-                const int kind = wq == 1 ? kF6T0 : wq == 2 ? kF6W2 : wq == 3 ? kF6Q0 : wq == 4 ? kF6T1
-                               : wq == 5 ? kF6W3 : -1;
-                if (kind >= 0 && wx * wy <= 36) {
-                    const int avail = 128 - wbits - (parts == 1 ? 17 : 29);
-                    const int cq = avail < 0 ? 0xFF : t.cquant[parts][avail];
-                    const int levels = kLevels[wq];
-                    e = kF6Lum | (wx == 6 && wy == 6 ? kF6Full : 0u) | (cq == 0xFF ? kF6Err : 0u) |
-                        (static_cast<uint32_t>(parts - 1) << 4) | (static_cast<uint32_t>(wq) << 6) |
-                        (static_cast<uint32_t>(cq == 0xFF ? 0 : cq) << 10) | (static_cast<uint32_t>(levels) << 15) |
-                        (static_cast<uint32_t>(kind) << 19) | (static_cast<uint32_t>(wbits) << 22);
-                }
-            }
-        }
-        f->info[v] = e;
-        // Header class (valid when every endpoint mode is 0; the kernel
-        // checks that and otherwise takes the runtime classifier).
-        uint8_t k = kC6Other;
-        if (e & kF6Const) {
-            k = kC6Const;
-        } else if (e & kF6Lum) {
-            if (e & kF6Err) {
-                k = kC6Const;  // error colour
-            } else if (!(e & kF6Full)) {
-                k = kC6Reduced;
-            } else {
-                for (int c = 0; c < kF6NumClasses; ++c)
-                    if (kF6Classes[c].wq == f6_wq(e) && kF6Classes[c].parts == f6_parts(e) &&
-                        kF6Classes[c].cq == f6_cq(e))
-                        k = static_cast<uint8_t>(kC6First + c);
-            }
-        }
-        // Bit 7: a luminance candidate (the class holds only with every
-        // endpoint mode 0).
-        f->klass[v] = static_cast<uint8_t>(k | ((e & kF6Lum) ? 0x80u : 0u));
-    }
-    for (int b = 0; b < 256; ++b)
-        for (int j = 0; j < 4; ++j) f->spread2[b] |= static_cast<uint32_t>((b >> (2 * j)) & 3) << (8 * j);
-    for (int b = 0; b < 4096; ++b)
-        for (int j = 0; j < 4; ++j) f->spread3[b] |= static_cast<uint32_t>((b >> (3 * j)) & 7) << (8 * j);
-    for (int Q = 0; Q < 128; ++Q) {
-        int d[3];
-        quint_digits(Q, d);
-        f->quint0[Q] = static_cast<uint32_t>(d[0] | (d[1] << 8) | (d[2] << 16));
-    }
-    for (int T = 0; T < 256; ++T) {
-        int d[5];
-        trit_digits(T, d);
-        f->trit0[T][0] = static_cast<uint32_t>(d[0] | (d[1] << 8) | (d[2] << 16) | (d[3] << 24));
-        f->trit0[T][1] = static_cast<uint32_t>(d[4]);
-    }
-    // A trit group with one plain bit per value: m0 T0 T1 m1 T2 T3 m2 T4 m3
-    // T5 T6 m4 T7 (bit 0 first); value j = 2 * trit j + m_j.
-    for (int w = 0; w < 8192; ++w) {
-        const int T = ((w >> 1) & 3) | (((w >> 4) & 3) << 2) | (((w >> 7) & 1) << 4) | (((w >> 9) & 3) << 5) |
-                      (((w >> 12) & 1) << 7);
-        const int m[5] = {w & 1, (w >> 3) & 1, (w >> 6) & 1, (w >> 8) & 1, (w >> 11) & 1};
-        int d[5];
-        trit_digits(T, d);
-        uint32_t lo = 0;
-        for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(2 * d[j] + m[j]) << (8 * j);
-        f->trit1[w][0] = lo;
-        f->trit1[w][1] = static_cast<uint32_t>(2 * d[4] + m[4]);
-    }
-}
-
 }  // namespace akv

@@ -65,60 +65,6 @@ struct Tables {
 // Fills `t` on the host. Deterministic; no device calls.
 void build_tables(Tables* t);
 
-// ---------------------------------------------------------------------------
-// Header decode of 6x6 luminance blocks by table, for the fused attention
-// kernel's common case (every astcenc 6x6 block of scalar KV data seen so far
-// is luminance-direct, single-plane, with a 6x6 or 5x6 / 6x5 weight grid and a
-// weight range of 0..2 to 0..7). The 11-bit block mode and the 2-bit
-// partition count fix everything else about such a block: the weight range,
-// the stream lengths and (with every endpoint mode 0) the colour range. One
-// lookup in `info` gives all of it, and each BISE group of the weight stream
-// is decoded by one lookup of its whole bit window into packed code bytes.
-
-// info[] entry layout.
-constexpr uint32_t kF6Lum = 1u << 0;    // luminance candidate: on the fast path when every endpoint mode is 0
-constexpr uint32_t kF6Const = 1u << 1;  // void extent or reserved mode: a constant block
-constexpr uint32_t kF6Err = 1u << 2;    // with endpoint mode 0 the colour data cannot fit: error colour
-constexpr uint32_t kF6Full = 1u << 3;   // full 6x6 weight grid (else a reduced grid)
-AKV_HD constexpr int f6_parts(uint32_t e) { return static_cast<int>((e >> 4) & 3) + 1; }
-AKV_HD constexpr int f6_wq(uint32_t e) { return static_cast<int>((e >> 6) & 15); }
-AKV_HD constexpr int f6_cq(uint32_t e) { return static_cast<int>((e >> 10) & 31); }
-AKV_HD constexpr int f6_levels(uint32_t e) { return static_cast<int>((e >> 15) & 15); }
-AKV_HD constexpr int f6_kind(uint32_t e) { return static_cast<int>((e >> 19) & 7); }
-AKV_HD constexpr int f6_wbits(uint32_t e) { return static_cast<int>((e >> 22) & 127); }
-// Weight stream kinds of the fast path: plain 2-bit and 3-bit codes, quints
-// (0..4), trits (0..2) and trits with one extra bit (0..5).
-enum : int { kF6W2 = 0, kF6W3 = 1, kF6Q0 = 2, kF6T0 = 3, kF6T1 = 4 };
-
-// Header classes of 6x6 blocks (Fast6Tables::klass): constant blocks, blocks
-// left to the runtime classifier, luminance blocks with a reduced grid, and
-// the luminance full-grid classes decoded by fully specialised code, each a
-// (weight range, partitions, colour range) triple. The colour range follows
-// from the other two (and the block mode) when every endpoint mode is 0.
-enum : int { kC6Const = 0, kC6Other = 1, kC6Reduced = 2, kC6First = 3 };
-struct F6Class {
-    int wq, parts, cq;
-};
-// Ordered by how often astcenc picks them for scalar KV data (the reference
-// corpus: 40 %, 26 %, 20 %, 5 % for the first four).
-constexpr F6Class kF6Classes[] = {{3, 2, 7},  {4, 1, 20}, {2, 3, 9},  {2, 2, 16}, {1, 4, 11},
-                                  {1, 3, 16}, {3, 1, 20}, {2, 1, 20}, {1, 1, 20}, {1, 2, 20}};
-constexpr int kF6NumClasses = static_cast<int>(sizeof(kF6Classes) / sizeof(kF6Classes[0]));
-constexpr int kC6Count = kC6First + kF6NumClasses;
-
-struct Fast6Tables {
-    uint32_t info[8192];         // (mode | (partitions - 1) << 11) -> info entry, 0 = not on the fast path
-    uint8_t klass[8192];         // the same index -> header class (kC6*) | 0x80 for luminance candidates
-    uint32_t spread2[256];       // four 2-bit fields -> four bytes
-    uint32_t spread3[4096];      // four 3-bit fields -> four bytes
-    uint32_t quint0[128];        // 7-bit quint block -> its three digits as bytes
-    uint32_t trit0[256][2];      // 8-bit trit block -> its five digits as bytes (4 + 1)
-    uint32_t trit1[8192][2];     // 13-bit group of a 0..5 stream -> its five codes as bytes (4 + 1)
-};
-
-// Fills `f` from the base tables `t` (which build_tables filled).
-void build_fast6_tables(const Tables& t, Fast6Tables* f);
-
 // Number of bits a BISE stream of `count` values of range `q` occupies.
 int bise_stream_bits(int count, int q);
 

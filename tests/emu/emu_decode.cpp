@@ -43,7 +43,6 @@ inline float __uint_as_float(unsigned int i) { float f; std::memcpy(&f, &i, 4); 
 inline unsigned int __float_as_uint(float f) { unsigned int i; std::memcpy(&i, &f, 4); return i; }
 #include "../../astc-kv_b200/csrc/akv_astc_device.cuh"
 #include "../../astc-kv_b200/csrc/akv_decode_fast.cuh"
-#include "../../astc-kv_b200/csrc/akv_decode6.cuh"
 
 extern "C" int emu_decode_blocks_u16(const uint8_t* blocks, int64_t n, int bs, uint16_t* out) {
     static bool ready = false;
@@ -226,92 +225,6 @@ extern "C" int emu_decode_rgba4(const uint8_t* blocks, int64_t n, float* out, in
             F::rgba_t4(r, codes, 1, t, tv);
             for (int k = 0; k < 4; ++k) o[4 * t + k] = tv[k] * 0x1p-16f;
         }
-    }
-    return 0;
-}
-
-// The attention kernel's 6x6 decode (akv_decode6.cuh), block by block as its
-// header phase handles them: the class lookup, then constant blocks,
-// specialised luminance classes (value table of unit values + per-texel entry
-// bytes, read back as the texel phase reads them), reduced grids (table
-// header decode, descriptor, then desc_seg_c16 as phase 1b evaluates it) and
-// everything else through the runtime path (fast_r_one).
-// cls: 100 + header class for the class paths, else the runtime path's kind.
-extern "C" int emu_decode_f6(const uint8_t* blocks, int64_t n, float* out, int* cls) {
-    static bool ready = false;
-    if (!ready) {
-        akv::build_tables(&akv::g_akv_tables);
-        akv::build_fast6_tables(akv::g_akv_tables, &akv::fast::g_f6);
-        ready = true;
-    }
-    namespace F = akv::fast;
-    for (int64_t i = 0; i < n; ++i) {
-        uint4 blk;
-        std::memcpy(&blk, blocks + 16 * i, 16);
-        float* o = out + i * 36;
-        int k = F::g_f6.klass[blk.x & 0x1FFFu];
-        if (k & 0x80) {
-            const bool cem0 = (blk.x & 0x1800u) == 0 ? ((blk.x >> 13) & 15) == 0 : ((blk.x >> 23) & 0x3F) == 0;
-            k = cem0 ? (k & 0x7F) : akv::kC6Other;
-        }
-        if (k == akv::kC6Other) {
-            const int rc = fast_r_one<6>(blk, cls + i, o);
-            if (rc) return rc;
-            continue;
-        }
-        cls[i] = 100 + k;
-        if (k == akv::kC6Const) {
-            const float u = akv::c16_to_unit(F::const_c16(blk));
-            for (int t = 0; t < 36; ++t) o[t] = u;
-            continue;
-        }
-        if (k >= akv::kC6First) {
-            uint32_t tab[12];
-            std::memset(tab, 0xEE, sizeof(tab));
-            uint32_t idx[9];
-            F::decode_class6_any(k - akv::kC6First, blk, false, 0.f, 0.f, tab, 1, idx,
-                                 std::make_integer_sequence<int, akv::kF6NumClasses>{});
-            const akv::F6Class c = akv::kF6Classes[k - akv::kC6First];
-            const int L = F::kLevelsCt[c.wq];
-            for (int t = 0; t < 36; ++t) {
-                const uint32_t e = F::byte_of(idx, t);
-                if (e >= static_cast<uint32_t>(c.parts * L)) return 4;
-                o[t] = __uint_as_float(tab[e]);
-            }
-            continue;
-        }
-        // Reduced grid through the table header decode and a descriptor.
-        uint8_t cscr[40];
-        std::memset(cscr, 0xEE, sizeof(cscr));
-        F::F6Lum d6;
-        F::decode_f6_lum(blk, F::g_f6.info[blk.x & 0x1FFFu], cscr, 1, d6);
-        const uint32_t me = akv::g_akv_tables.mode[1][blk.x & 0x7FFu];
-        const int wx = akv::mode_wx(me), wy = akv::mode_wy(me);
-        akv::BlockDesc<1> d;
-        if (d6.parts > 1) {
-            const uint32_t* pt = akv::g_akv_tables.part[1][d6.parts - 2][(blk.x >> 13) & 0x3FF];
-            d.pat[0] = pt[0]; d.pat[1] = pt[1]; d.pat_hi[0] = pt[2]; d.pat_hi[1] = pt[3];
-        } else {
-            d.pat[0] = d.pat[1] = d.pat_hi[0] = d.pat_hi[1] = 0u;
-        }
-        d.ep[0] = static_cast<uint32_t>(d6.v[0] | (d6.v[2] << 8) | (d6.v[4] << 16) | (d6.v[6] << 24));
-        d.ep[1] = static_cast<uint32_t>(d6.v[1] | (d6.v[3] << 8) | (d6.v[5] << 16) | (d6.v[7] << 24));
-        d.info = static_cast<uint32_t>(d6.parts - 1) | (1u << akv::kInfoReduced) |
-                 (static_cast<uint32_t>(wx) << akv::kInfoWx) | (static_cast<uint32_t>(wy) << akv::kInfoWy);
-        uint8_t codes[40];
-        for (int j = 0; j < 36; ++j) codes[j] = static_cast<uint8_t>(F::byte_of(d6.cw, j));
-        alignas(16) uint8_t w[72];
-        std::memset(w, 0xEE, sizeof(w));
-        for (int q = 0; q < 8 * wy; ++q)
-            if ((q & 7) < wx) w[q] = F::desc_weight(codes, 1, akv::g_akv_tables.wunq[d6.wq], wx, q);
-        constexpr int SEG = F::kDescSeg<6>;
-        for (int y = 0; y < 6; ++y)
-            for (int x0 = 0; x0 < 6; x0 += SEG) {
-                uint32_t c[SEG];
-                F::desc_seg_c16<6, SEG>(d.info, w, akv::row_pattern<6>(d.pat[0], d.pat[1], d.pat_hi[0], d.pat_hi[1], y),
-                                        d.ep[0], d.ep[1], y, x0, c);
-                for (int x = 0; x < SEG; ++x) o[y * 6 + x0 + x] = akv::c16_to_unit(c[x]);
-            }
     }
     return 0;
 }

@@ -141,40 +141,3 @@ def test_rgba4_fast_decode_matches_oracle(source):
     if source == "encoder":
         assert (cls == 0).mean() > 0.9  # the encoder's RGBA blocks take the fast path
     np.testing.assert_array_equal(got, ref)
-
-
-@pytest.mark.parametrize("source", ["golden", "story", "random", "garbage", "encoder"])
-def test_f6_class_decode_matches_oracle(source):
-    """The attention kernel's 6x6 decode (class lookup; specialised classes
-    with colour and weight groups at compile-time positions, weight groups by
-    window lookups into code bytes, per-texel entry bytes from codes + L *
-    partition; reduced grids through the descriptor evaluator; the runtime
-    path for the rest) against the oracle's fp16 view, bit for bit. The
-    reference's astcenc blocks must nearly all take the class paths."""
-    from astc_kv_cuda.ops import host_encode, random_blocks
-    if source == "golden":
-        blocks = golden("block_geometry_identity")["blocks"].reshape(-1, 16)
-    elif source == "story":
-        blocks = golden("story_l17_v_token6")["v_blocks"].reshape(-1, 16)
-    elif source == "random":
-        blocks = random_blocks(30000, 6, seed=70)
-    elif source == "garbage":
-        blocks = np.random.default_rng(71).integers(0, 256, (30000, 16), dtype=np.uint8)
-    else:
-        x = np.random.default_rng(72).random((6 * 30, 6 * 22), np.float32)
-        x = np.repeat(x[..., None], 4, -1)
-        x[..., 3] = 1
-        blocks = np.frombuffer(host_encode(x, 6, "scalar", 1), np.uint8).reshape(-1, 16)
-    lib = ct.CDLL(str(EMU))
-    lib.emu_decode_f6.argtypes = [ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]
-    b = np.ascontiguousarray(blocks, np.uint8)
-    got = np.empty((b.shape[0], 36), np.float32)
-    cls = np.empty(b.shape[0], np.int32)
-    assert lib.emu_decode_f6(b.ctypes.data, b.shape[0], got.ctypes.data, cls.ctypes.data) == 0
-    ref = O.decode_blocks(b, 6, O.OUT_FP16, threads=4)[..., 0].reshape(b.shape[0], 36).astype(np.float32)
-    np.testing.assert_array_equal(got, ref)
-    if source in ("golden", "story"):
-        # A few astcenc blocks use wider weight ranges (0..9 and up) and take
-        # the runtime path; the rest take the class paths (100 + class:
-        # 100 constant, 102 reduced grid, 103.. the specialised full grids).
-        assert (cls >= 103).mean() > 0.9 and (cls >= 100).mean() > 0.99, np.unique(cls, return_counts=True)
