@@ -20,11 +20,13 @@
 //   * Tensor cores (mma.sync m16n8k16, fp32 accumulation). Every warp owns
 //     one (16-token tile, half of the head dims) pair; the query heads of
 //     the GQA group are the N=8 dimension:
-//       S^T[tok][head] = K . Q^T   (q hi+lo; FP16 K staged in shared memory
-//                                   by 16-byte cp.async copies issued a
-//                                   chunk ahead (they land during the
-//                                   chunk's decode), or decoded K hi+lo;
-//                                   both warps of a tile compute it)
+//       S^T[tok][head] = K . Q^T   (q hi+lo; FP16 K either straight from
+//                                   global memory in fragment order,
+//                                   L2-prefetched a chunk ahead (6x6 V), or
+//                                   staged in shared memory by 16-byte
+//                                   cp.async copies issued a chunk ahead
+//                                   (4x4 / 8x8 V); or decoded K hi+lo; both
+//                                   warps of a tile compute it)
 //       online softmax per head in base 2, P^T as fp16 through a 256-byte
 //       per-warp buffer,
 //       O^T[dim][head] += V^T . P^T  for the warp's dim half (V hi and lo,
@@ -194,7 +196,7 @@ struct DecodeScratch {
     // Descriptor slots: every block of a small chunk (8x8 planes are mostly
     // reduced grids), at most 64; 40 for 6x6 planes (astcenc's 6x6 chunks
     // hold about ten descriptor blocks in 176).
-    static constexpr int kSlowMax = BS == 6 ? 40 : 64;
+    static constexpr int kSlowMax = 64;
     static constexpr int kSlowCap = NB < kSlowMax ? NB : kSlowMax;
     // Columns: one per decoding thread (a chunk with fewer blocks than
     // threads leaves the others idle).
@@ -672,6 +674,16 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
+    // FP16 K with a 6x6 V plane: K fragments straight from global memory
+    // (L2-prefetched a chunk ahead), which leaves the shared memory to the
+    // decoder and L1 (measured on config 2: 4.65 ms against 4.77 with the K
+    // rows staged); other FP16-K instances stage the rows by cp.async
+    // (config 4's 4x4 V: 7.87 ms against 8.22).
+    static constexpr bool KDIRECT = KBS == 0 && VBS == 6;
+    // CTAs per SM (shared memory allows three; scalar 4x4 V with FP16 K runs
+    // two with more registers), and the register cap that fits them.
+    static constexpr int CTAS = (VBS == 4 && KBS == 0 && VL == AKV_LAYOUT_SCALAR) ? 2 : 3;
+    static constexpr int MAXREG = (65536 / (CTAS * THREADS)) / 8 * 8;
     static constexpr size_t VDS = sizeof(DecodeScratch<VBLK, THREADS, VBS>);
     static constexpr size_t KDS = KBS ? sizeof(DecodeScratch<(KBS ? KBLK : 1), THREADS, (KBS ? KBS : 4)>) : 0;
     static constexpr size_t DSBYTES = VDS > KDS ? VDS : KDS;     // decode scratch, shared by the planes
@@ -688,6 +700,7 @@ struct Smem {
     using C = Cfg<D, G, VBS, KBS, VL>;
     uint64_t bar[2];
     int valid[2];
+    int stuck_c;  // chunk whose copies did not arrive in time
     __align__(16) uint4 vraw[2][C::VBLK];
     __align__(16) __half vmeta[2][2][C::META];
     __align__(16) uint4 kraw[2][KBS ? C::KBLK : 1];
@@ -695,7 +708,7 @@ struct Smem {
     __align__(16) __half kside[2][KBS ? C::SIDE : 1];
     __align__(16) __half vhi[C::CH][C::LD];
     __align__(16) __half vlo[C::CH][C::LD];
-    __align__(16) __half khi[C::CH][C::LD];   // decoded K hi, or the staged FP16 K rows
+    __align__(16) __half khi[(KBS || !C::KDIRECT) ? C::CH : 1][C::LD];  // decoded K hi, or staged FP16 K rows
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[2 * C::NWM][8][16];
@@ -707,10 +720,10 @@ struct Smem {
 
 // Three CTAs per SM, except scalar 4x4 V with FP16 K (256 threads): two CTAs
 // with up to 128 registers instead of spilling at 80 (C4 9.7 ms against 10.5;
-// the RGBA 4x4 instances are faster with three).
+// the RGBA 4x4 instances are faster with three). The register cap is the
+// most the CTAs per SM leave (Cfg::MAXREG).
 template <int D, int G, int VBS, int KBS, int VL = AKV_LAYOUT_SCALAR>
-__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
-                                  (VBS == 4 && KBS == 0 && VL == AKV_LAYOUT_SCALAR) ? 2 : 3)
+__global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VBS, KBS, VL>::CTAS)
     attn_fast_kernel(AttnParams p) {
     using C = Cfg<D, G, VBS, KBS, VL>;
     using S = Smem<D, G, VBS, KBS, VL>;
@@ -815,7 +828,12 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         const int64_t qb = (static_cast<int64_t>(b) * p.Hq + h * G + (has ? qn : 0)) * D;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-            const int d0 = 16 * ks + 2 * qj, d1 = d0 + 8;
+            // Natural dim order for shared-memory K; a permuted order for
+            // direct FP16 K loads (lane quad j of a row loads dims
+            // [32 g + 8 j, 32 g + 8 j + 8) of each 32-dim group g).
+            int d0, d1;
+            if (!C::KDIRECT) { d0 = 16 * ks + 2 * qj; d1 = d0 + 8; }
+            else { const int g32 = ks >> 1, half = ks & 1; d0 = 32 * g32 + 8 * qj + 4 * half; d1 = d0 + 2; }
             const float q0 = has ? load_q(p.q, p.q_dtype, qb + d0) : 0.f;
             const float q1 = has ? load_q(p.q, p.q_dtype, qb + d0 + 1) : 0.f;
             const float q2 = has ? load_q(p.q, p.q_dtype, qb + d1) : 0.f;
@@ -830,29 +848,60 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
     // FP16 K rows of chunk c -> sm.khi by 16-byte asynchronous copies (rows
     // past the split or on unmapped pages copy zero bytes: zeros).
     auto stage_k = [&](int c) {
-        if constexpr (KBS == 0) {
+        if constexpr (KBS == 0 && !C::KDIRECT) {
             constexpr int PPR = D / 8, PIECES = CH * PPR;
             const int t0 = t_begin + c * CH;
             const uint8_t* kbase = p.k.data + b * p.k.sB + h * p.k.sH;
-            for (int piece = tid; piece < PIECES; piece += THREADS) {
-                const int r = piece / PPR, j = piece - r * PPR;
-                const int t = t0 + r;
-                const int phys = t < t_end ? phys_page(p.table, p.pps, p.num_pages, b, t / P, nullptr) : -1;
-                const uint8_t* src =
-                    phys >= 0 ? kbase + static_cast<int64_t>(phys) * p.k.sP + static_cast<int64_t>(t % P) * (D * 2) + j * 16
-                              : kbase;
-                cp_async16(&sm.khi[r][8 * j], src, phys >= 0 ? 16u : 0u);
+            if (P % CH == 0) {
+                // The chunk lies in one page: one table lookup, contiguous rows.
+                const int page = t0 / P;
+                const int phys = phys_page(p.table, p.pps, p.num_pages, b, page, nullptr);
+                const int nrow = phys >= 0 ? min(CH, t_end - t0) : 0;
+                const uint8_t* src0 = phys >= 0 ? kbase + static_cast<int64_t>(phys) * p.k.sP +
+                                                      static_cast<int64_t>(t0 - page * P) * (D * 2)
+                                                : kbase;
+                for (int piece = tid; piece < PIECES; piece += THREADS) {
+                    const int r = piece / PPR;
+                    const bool ok = r < nrow;
+                    cp_async16(&sm.khi[r][8 * (piece - r * PPR)], ok ? src0 + static_cast<int64_t>(piece) * 16 : kbase,
+                               ok ? 16u : 0u);
+                }
+            } else {
+                for (int piece = tid; piece < PIECES; piece += THREADS) {
+                    const int r = piece / PPR, j = piece - r * PPR;
+                    const int t = t0 + r;
+                    const int phys = t < t_end ? phys_page(p.table, p.pps, p.num_pages, b, t / P, nullptr) : -1;
+                    const uint8_t* src = phys >= 0 ? kbase + static_cast<int64_t>(phys) * p.k.sP +
+                                                         static_cast<int64_t>(t % P) * (D * 2) + j * 16
+                                                   : kbase;
+                    cp_async16(&sm.khi[r][8 * j], src, phys >= 0 ? 16u : 0u);
+                }
             }
             cp_async_commit();
         }
     };
+    // Direct K: L2 prefetch of chunk c's rows (one warp per token tile).
+    auto prefetch_k = [&](int c) {
+        if constexpr (C::KDIRECT) {
+            if (dh == 0 && c < nchunks) {
+                const int tt = t_begin + c * CH + 16 * tw + (lane >> 1);
+                if (tt < t_end && (lane & 1) * 128 < D * 2) {
+                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
+                    if (phys >= 0)
+                        prefetch_l2(p.k.data + b * p.k.sB + h * p.k.sH + static_cast<int64_t>(phys) * p.k.sP +
+                                    static_cast<int64_t>(tt % P) * D * 2 + (lane & 1) * 128);
+                }
+            }
+        }
+    };
     stage_k(0);
+    prefetch_k(0);
 
     float o[KH][4];
 #pragma unroll
     for (int i = 0; i < KH; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F}, l_run[2] = {0.f, 0.f};
-    int stuck = -1;  // chunk whose copies did not arrive in time
+    bool stuck = false;  // a chunk's copies did not arrive in time (its index: sm.stuck_c)
 
     for (int c = 0; c < nchunks; ++c) {
         const int s = c & 1;
@@ -861,10 +910,12 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         const int n = min(CH, t_end - t0);
         const bool waited = mbar_wait(&sm.bar[s], parity);
         if (__syncthreads_or(!waited)) {
-            stuck = c;
+            stuck = true;
+            if (tid == 0) sm.stuck_c = c;
             break;
         }
         const bool valid = sm.valid[s] != 0;
+        prefetch_k(c + 1);
         // Decode V (and K) tiles.
         if constexpr (VL == AKV_LAYOUT_RGBA)
             decode_plane_rgba<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
@@ -915,10 +966,31 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
             }
             __syncthreads();
         }
-        if constexpr (KBS == 0) {
+        if constexpr (KBS == 0 && !C::KDIRECT) {
             // This chunk's K rows have landed (issued a chunk ahead).
             cp_async_wait<0>();
             __syncthreads();
+        }
+        // Direct FP16 K fragments for this warp's 16 tokens (loaded after the
+        // decode so they do not hold registers through it), permuted dims.
+        uint4 kreg[C::KDIRECT ? D / 32 : 1][2];
+        if constexpr (C::KDIRECT) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int tr = 16 * tw + qn + 8 * rr;
+                const int tt = t0 + tr;
+                const uint4* row = nullptr;
+                if (tr < n) {
+                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
+                    if (phys >= 0)
+                        row = reinterpret_cast<const uint4*>(p.k.data + b * p.k.sB + h * p.k.sH +
+                                                             static_cast<int64_t>(phys) * p.k.sP +
+                                                             static_cast<int64_t>(tt % P) * D * 2);
+                }
+#pragma unroll
+                for (int g32 = 0; g32 < D / 32; ++g32)
+                    kreg[g32][rr] = row ? __ldg(row + 4 * g32 + qj) : make_uint4(0u, 0u, 0u, 0u);
+            }
         }
         // The raw stage is consumed: refill it with chunk c + 2.
         if (tid == 0 && c + 2 < nchunks) {
@@ -936,15 +1008,24 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
                 const uint4 qf = sm.qfrag[ks][lane];
                 float* acc = sa[ks & 1];
                 uint32_t a[4];
-                const int mi = lane >> 3, rr = lane & 7;
-                const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
-                const int col = 16 * ks + ((mi & 2) ? 8 : 0);
-                ldsm_x4(a, &sm.khi[row][col]);
-                mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
-                if constexpr (KBS > 0) {
-                    ldsm_x4(a, &sm.klo[row][col]);
+                if constexpr (C::KDIRECT) {
+                    const uint4 r0 = kreg[ks >> 1][0];
+                    const uint4 r1 = kreg[ks >> 1][1];
+                    if ((ks & 1) == 0) { a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y; }
+                    else { a[0] = r0.z; a[2] = r0.w; a[1] = r1.z; a[3] = r1.w; }
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
+                } else {
+                    const int mi = lane >> 3, rr = lane & 7;
+                    const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
+                    const int col = 16 * ks + ((mi & 2) ? 8 : 0);
+                    ldsm_x4(a, &sm.khi[row][col]);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
+                    if constexpr (KBS > 0) {
+                        ldsm_x4(a, &sm.klo[row][col]);
+                        mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                    }
                 }
             }
             float sacc[4];
@@ -1012,17 +1093,18 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS,
         __syncthreads();  // tiles and P buffers free for the next chunk
         if (c + 1 < nchunks) stage_k(c + 1);
     }
-    if constexpr (KBS == 0) cp_async_wait<0>();  // nothing in flight past the loop
+    if constexpr (KBS == 0 && !C::KDIRECT) cp_async_wait<0>();  // nothing in flight past the loop
 
-    if (stuck >= 0) {
+    if (stuck) {
         // A copy never completed: report, give the copies still in flight
         // (chunk `stuck` and, if it was issued, chunk stuck + 1, one per
         // stage) a bounded grace period each so none lands in shared memory
         // after the CTA exits, and leave this split empty.
         if (tid == 0) {
             if (p.status) atomicExch(p.status, AKV_ERR_TIMEOUT);
-            mbar_wait(&sm.bar[stuck & 1], (stuck >> 1) & 1);
-            if (stuck + 1 < nchunks) mbar_wait(&sm.bar[(stuck + 1) & 1], ((stuck + 1) >> 1) & 1);
+            const int sc = sm.stuck_c;
+            mbar_wait(&sm.bar[sc & 1], (sc >> 1) & 1);
+            if (sc + 1 < nchunks) mbar_wait(&sm.bar[(sc + 1) & 1], ((sc + 1) >> 1) & 1);
         }
         __syncthreads();
         for (int i = tid; i < G * D; i += THREADS)
