@@ -265,28 +265,108 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnParams p) 
     }
 }
 
-// LSE merge: one CTA per (query head, batch), threads over channels.
-__global__ void merge_kernel(AttnParams p, int D) {
-    const int hq = blockIdx.x, b = blockIdx.y;
+constexpr int kMergeThreads = 512;
+// Split weights the merge keeps in dynamic shared memory (44 KB, inside the
+// 48 KB a launch gets without opting in); beyond that it recomputes them per
+// dimension.
+constexpr int kMergeSmemSplits = 11 * 1024;
+
+// Block-wide max / sum of one value per thread, in a fixed order (the result
+// does not depend on thread timing). `red` holds 32 floats.
+__device__ __forceinline__ float block_max(float v, float* red) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < nw; ++w) r = fmaxf(r, red[w]);
+    return r;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < nw; ++w) r += red[w];
+    return r;
+}
+
+// Combines the split partials of one (query head, sequence):
+// out = sum_s w_s acc_s / sum_s w_s l_s with w_s = 2^(m_s - max_s m_s); empty
+// splits (m = -inf) weigh 0, also when every split is empty, so nothing to
+// attend gives zeros. The weights are computed once per split (into shared
+// memory when wcap covers the splits); each dimension's sum is split into
+// blockDim / D phases over the splits, each phase loading eight splits at a
+// time (the merge is bound by load latency, not bandwidth), added in a
+// fixed order.
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(AttnParams p, int D, int wcap) {
+    extern __shared__ float wsm[];  // [wcap] split weights
+    __shared__ float red[32];
+    __shared__ float part[kMergeThreads];
+    const int hq = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
     const int len = seq_len_of(p, b);
     const int ns = p.merge_all ? p.split_stride : min(p.nsplits, (len + p.split_tokens - 1) / p.split_tokens);
     const int64_t unit0 = (static_cast<int64_t>(b) * p.Hq + hq) * p.split_stride;
-    float M = -CUDART_INF_F;
-    for (int s = 0; s < ns; ++s) M = fmaxf(M, p.part_ml[(unit0 + s) * 2]);
-    // Weight of split s; empty splits (m = -inf) weigh 0, also when every
-    // split is empty (M = -inf), so nothing to attend gives zeros.
+    const float* ml = p.part_ml + unit0 * 2;
+    float m = -CUDART_INF_F;
+    for (int s = tid; s < ns; s += blockDim.x) m = fmaxf(m, ml[2 * s]);
+    const float M = block_max(m, red);
     auto weight = [&](int s) {
-        const float m = p.part_ml[(unit0 + s) * 2];
-        return m == -CUDART_INF_F ? 0.f : exp2f(m - M);
+        const float ms = ml[2 * s];
+        return ms == -CUDART_INF_F ? 0.f : exp2f(ms - M);
     };
-    float den = 0.f;
-    for (int s = 0; s < ns; ++s) den += weight(s) * p.part_ml[(unit0 + s) * 2 + 1];
-    const float inv = (ns > 0 && den > 0.f) ? 1.f / den : 0.f;
-    for (int c = threadIdx.x; c < D; c += blockDim.x) {
-        float num = 0.f;
-        for (int s = 0; s < ns; ++s) num += weight(s) * p.part_acc[(unit0 + s) * D + c];
-        p.out[(static_cast<int64_t>(b) * p.Hq + hq) * D + c] = num * inv;
+    float dpart = 0.f;
+    for (int s = tid; s < ns; s += blockDim.x) {
+        const float w = weight(s);
+        if (s < wcap) wsm[s] = w;
+        dpart += w * ml[2 * s + 1];
     }
+    const float den = block_sum(dpart, red);  // its barriers also publish wsm
+    const float inv = (ns > 0 && den > 0.f) ? 1.f / den : 0.f;
+    const float* acc = p.part_acc + unit0 * D;
+    float* out = p.out + (static_cast<int64_t>(b) * p.Hq + hq) * D;
+    if (D <= static_cast<int>(blockDim.x)) {
+        const int nph = blockDim.x / D, c = tid % D, ph = tid / D;
+        float num = 0.f;
+        if (ph < nph) {
+            auto w = [&](int sp) { return sp < wcap ? wsm[sp] : weight(sp); };
+            float n[4] = {0.f, 0.f, 0.f, 0.f};
+            int sp = ph;
+            for (; sp + 7 * nph < ns; sp += 8 * nph) {
+                float a[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) a[k] = acc[static_cast<int64_t>(sp + k * nph) * D + c];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) n[k & 3] += w(sp + k * nph) * a[k];
+            }
+            for (; sp < ns; sp += nph) n[0] += w(sp) * acc[static_cast<int64_t>(sp) * D + c];
+            num = (n[0] + n[1]) + (n[2] + n[3]);
+        }
+        part[tid] = num;
+        __syncthreads();
+        if (tid < D) {
+            float t = part[tid];
+            for (int q = 1; q < nph; ++q) t += part[q * D + tid];
+            out[tid] = t * inv;
+        }
+    } else {
+        for (int c = tid; c < D; c += blockDim.x) {
+            float num = 0.f;
+            for (int s = 0; s < ns; ++s) num += (s < wcap ? wsm[s] : weight(s)) * acc[static_cast<int64_t>(s) * D + c];
+            out[c] = num * inv;
+        }
+    }
+}
+
+// Launches merge_kernel for every (query head, sequence) of p.
+inline void launch_merge(const AttnParams& p, int D, cudaStream_t s) {
+    const int ns = p.merge_all ? p.split_stride : p.nsplits;
+    const int wcap = ns <= kMergeSmemSplits ? ns : 0;
+    merge_kernel<<<dim3(p.Hq, p.B), kMergeThreads, static_cast<size_t>(wcap) * sizeof(float), s>>>(p, D, wcap);
 }
 
 }  // namespace akv

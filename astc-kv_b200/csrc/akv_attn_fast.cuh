@@ -27,8 +27,8 @@
 //                                   cp.async copies issued a chunk ahead
 //                                   (4x4 / 8x8 V); or decoded K hi+lo; both
 //                                   warps of a tile compute it)
-//       online softmax per head in base 2, P^T as fp16 through a 256-byte
-//       per-warp buffer,
+//       online softmax per head in base 2, P^T as fp16 hi + lo through a
+//       512-byte per-warp buffer,
 //       O^T[dim][head] += V^T . P^T  for the warp's dim half (V hi and lo,
 //                                     ldmatrix.trans).
 //   * Each warp keeps its own (m, l, O half) over its token slices; the
@@ -108,9 +108,11 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
 }
 
+// A register-only operation (no memory, no side effects): not volatile, so
+// the compiler may interleave independent accumulator chains.
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -120,6 +122,12 @@ __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uin
 __device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
                  : "r"(smem_u32(p)));
 }
 
@@ -711,7 +719,7 @@ struct Smem {
     __align__(16) __half khi[(KBS || !C::KDIRECT) ? C::CH : 1][C::LD];  // decoded K hi, or staged FP16 K rows
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
-    __align__(16) __half pbuf[2 * C::NWM][8][16];
+    __align__(16) __half pbuf[2 * C::NWM][2][16][8];  // per warp: P hi, P lo as [token][head]
     __align__(16) uint4 qfrag[D / 16][32];                         // per lane: q hi (2 words) | q lo (2 words)
 
     float wm[C::NWM][8];
@@ -1066,16 +1074,25 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
                 o[i][2] *= alpha[0];
                 o[i][3] *= alpha[1];
             }
-            // P^T -> per-warp buffer as P[head][tok] (fp16), then B fragments.
-            __half(*pb)[16] = sm.pbuf[warp];
-            pb[2 * qj][qn] = __float2half_rn(sv[0]);
-            pb[2 * qj + 1][qn] = __float2half_rn(sv[1]);
-            pb[2 * qj][qn + 8] = __float2half_rn(sv[2]);
-            pb[2 * qj + 1][qn + 8] = __float2half_rn(sv[3]);
+            // P^T -> per-warp buffers as [token][head] in fp16 hi + lo (the
+            // unrounded p is what l accumulates); ldmatrix.trans gives the B
+            // fragments (k = token, n = head).
+            __half(*pbh)[8] = sm.pbuf[warp][0];
+            __half(*pbl)[8] = sm.pbuf[warp][1];
+            {
+                const __half2 h01 = __floats2half2_rn(sv[0], sv[1]), h23 = __floats2half2_rn(sv[2], sv[3]);
+                const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                *reinterpret_cast<__half2*>(&pbh[qn][2 * qj]) = h01;
+                *reinterpret_cast<__half2*>(&pbh[qn + 8][2 * qj]) = h23;
+                *reinterpret_cast<__half2*>(&pbl[qn][2 * qj]) = __floats2half2_rn(sv[0] - f01.x, sv[1] - f01.y);
+                *reinterpret_cast<__half2*>(&pbl[qn + 8][2 * qj]) = __floats2half2_rn(sv[2] - f23.x, sv[3] - f23.y);
+            }
             __syncwarp();
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&pb[qn][2 * qj]);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&pb[qn][2 * qj + 8]);
-            // O^T[dim][head] += V^T . P^T with V = hi + lo.
+            uint32_t b0, b1, b0l, b1l;
+            ldsm_x2_t(b0, b1, &pbh[lane & 15][0]);
+            ldsm_x2_t(b0l, b1l, &pbl[lane & 15][0]);
+            // O^T[dim][head] += V^T . P^T with V = hi + lo and P = hi + lo
+            // (the lo x lo product, below 2^-22 relative, is left out).
             const int mi = lane >> 3, rr = lane & 7;
             const int vrow = 16 * tw + rr + ((mi & 2) ? 8 : 0);
             const int vcol = (mi & 1) ? 8 : 0;
@@ -1085,6 +1102,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
                 uint32_t a[4];
                 ldsm_x4_t(a, &sm.vhi[vrow][16 * dt + vcol]);
                 mma16816(o[mt], a[0], a[1], a[2], a[3], b0, b1);
+                mma16816(o[mt], a[0], a[1], a[2], a[3], b0l, b1l);
                 ldsm_x4_t(a, &sm.vlo[vrow][16 * dt + vcol]);
                 mma16816(o[mt], a[0], a[1], a[2], a[3], b0, b1);
             }

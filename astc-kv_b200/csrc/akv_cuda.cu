@@ -141,7 +141,7 @@ int launch_attention(const AttnParams& p, cudaStream_t s, int phases) {
         if (int st = launch_status()) return st;
     }
     if (phases & AKV_PHASE_MERGE) {
-        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        launch_merge(p, D, s);
         if (int st = launch_status()) return st;
     }
     return AKV_OK;
@@ -164,7 +164,7 @@ int launch_fast(const AttnParams& p, cudaStream_t s, int phases) {
         if (int st = launch_status()) return st;
     }
     if (phases & AKV_PHASE_MERGE) {
-        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        launch_merge(p, D, s);
         if (int st = launch_status()) return st;
     }
     return AKV_OK;
@@ -204,7 +204,7 @@ int launch_fp16(const AttnParams& p, cudaStream_t s, int phases) {
         if (int st = launch_status()) return st;
     }
     if (phases & AKV_PHASE_MERGE) {
-        merge_kernel<<<dim3(p.Hq, p.B), 128, 0, s>>>(p, D);
+        launch_merge(p, D, s);
         if (int st = launch_status()) return st;
     }
     return AKV_OK;
@@ -246,6 +246,8 @@ bool fp16_path_ok(const AkvAttnDesc* d) {
         if (pl->stride_batch % 16 || pl->stride_head % 16 || pl->stride_page % 16) return false;
     return true;
 }
+
+constexpr int kMinSplitChunks = 6;
 
 int fast_chunk(int kbs, int vbs) { return (vbs == 6 || kbs == 6) ? 48 : (kbs ? 32 : 64); }
 
@@ -406,10 +408,18 @@ int plan_attention(const AkvAttnDesc* d, AttnPlan* out, size_t ws_limit = 0) {
         // splits keep the SMs evenly busy to the end of the launch (measured
         // against 8 per SM: C2 5.06 -> 4.76 ms, C3 11.2 -> 10.1, C4 9.6 ->
         // 8.2), for a split-partial workspace that grows with the count.
+        // Splits of at least kMinSplitChunks chunks: when few (head, batch)
+        // units share the GPU (one KV head per GPU of eight), shorter splits
+        // cost more in per-split set-up and merge work than they gain in
+        // balance (config 2 at one head per GPU: 0.695 ms with 3-chunk splits,
+        // 0.670 with 6).
         const int64_t units = static_cast<int64_t>(d->batch) * d->kv_heads;
         const int64_t want = (static_cast<int64_t>(sm_count()) * 64 + units - 1) / units;
         int64_t per = (d->max_tokens + want - 1) / want;
         per = ((per + ch - 1) / ch) * ch;
+        const int64_t min_per = static_cast<int64_t>(kMinSplitChunks) * ch;
+        const int64_t whole = ((d->max_tokens + ch - 1) / ch) * ch;
+        if (per < min_per) per = min_per < whole ? min_per : whole;
         split = static_cast<int>(per < ch ? ch : per);
     }
     int lcm_fp = out->kbs ? out->kbs : 1;
@@ -647,7 +657,7 @@ int akv_cuda_decode_attention_tail(const AkvAttnDesc* d, const AkvAttnDesc* tail
     if (int st = launch_segment(tail, b, pb, s, AKV_PHASE_SPLIT)) return st;
     // One merge over both segments' split rows (empty splits hold m = -inf).
     pa.merge_all = 1;
-    merge_kernel<<<dim3(pa.Hq, pa.B), 128, 0, s>>>(pa, d->head_dim);
+    launch_merge(pa, d->head_dim, s);
     return launch_status();
 }
 

@@ -642,6 +642,9 @@ def run_ours(args) -> dict | None:
     A.init(local)
     shard = "replica" if args.shard == "replica" or args.batch else SHARD[args.workload]
     units = rank_units(args.workload, rank, world, shard)
+    if args.shard_of > 1 and world == 1 and shard != "replica":
+        # Rank 0's share of an N-GPU job on one GPU (profiling the per-rank work).
+        units = rank_units(args.workload, 0, args.shard_of, shard)
     wl = Workload(args.workload, dev, units=units, batch=args.batch, split_tokens=args.split_tokens)
     stream = torch.cuda.current_stream()
 
@@ -706,6 +709,8 @@ def run_ours(args) -> dict | None:
         cfg["batch_override"] = args.batch
     if args.split_tokens:
         cfg["split_tokens"] = args.split_tokens
+    if args.shard_of > 1 and world == 1:
+        cfg["shard_of"] = f"rank 0's share of a {args.shard_of}-GPU job"
     line = {
         "metric": METRIC, "value": toks / (total_ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
@@ -1017,6 +1022,8 @@ def main():
     ap.add_argument("--decode-blocks", type=int, default=1 << 26,
                     help="blocks per step of the decode microbench (a multiple of 2^20; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="on one GPU, run only rank 0's shard of an N-GPU job (profiling the per-rank work)")
     ap.add_argument("--per-layer", action="store_true",
                     help="c1 only: time one attention call per layer (eager and as one CUDA graph) next to the "
                          "single 30-layer launch")

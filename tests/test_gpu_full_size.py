@@ -83,11 +83,15 @@ def _run(wl) -> np.ndarray:
     return out.cpu().numpy()
 
 
-def test_config2_full_size_bench_inputs(cuda):
+@pytest.mark.parametrize("split", [0, 912])
+def test_config2_full_size_bench_inputs(cuda, split):
     """Config 2 as benchmarked, one sequence: T 32768, Hq32/Hkv8, bf16 q, FP16
-    K, astcenc 6x6 golden rows tiled with a random block affine, default split."""
+    K, astcenc 6x6 golden rows tiled with a random block affine; the default
+    split for one sequence (48 tokens), and the 912-token splits the batch-32
+    benchmark line uses (19 chunks rescaled online per split, 36 splits
+    merged)."""
     import bench
-    wl = bench.Workload("c2", cuda, batch=1)
+    wl = bench.Workload("c2", cuda, batch=1, split_tokens=split)
     got = _run(wl)
     pu = _pool_rows_u(bench.pool("c2v"), 6, "scalar")  # [R, 6, 66]
     idx = wl.host["idx"][0].cpu().numpy()  # [H, rows, 2]
@@ -100,7 +104,7 @@ def test_config2_full_size_bench_inputs(cuda):
         u = np.concatenate([pu[idx[h, :, 0]], pu[idx[h, :, 1]]], axis=-1).reshape(-1, 132)
         v = _affine(u, off[h], scl[h], 6)[:T, :D]
         ref[h * G:(h + 1) * G] = _attn_head(q[h * G:(h + 1) * G], k[h, :T], v)
-    _report("config2 B1 T32768 (bench inputs)", got[0], ref, wl.attn.plan())
+    _report(f"config2 B1 T32768 (bench inputs, split {split or 'default'})", got[0], ref, wl.attn.plan())
 
 
 def test_config2_fp16_control_full_size(cuda):

@@ -96,8 +96,8 @@ def test_noalloc_matches_workspace_entry_point(cuda):
 def test_noalloc_default_split_fits_the_static_array(cuda):
     """split_tokens = 0 leaves the split to the library, which then picks one
     whose partials fit the static array; the result still matches the oracle.
-    The second case is config 2's shape (Hq32/Hkv8, D128) at one sequence of
-    32768 tokens, whose usual split would need about 11 MB of partials."""
+    The second case is config 2's shape (Hq32/Hkv8, D128) at eight sequences
+    of 32768 tokens, whose usual split would need about 15 MB of partials."""
     attn, expect = _case()
     for call in range(2):
         attn.out.fill_(float("nan"))
@@ -108,7 +108,7 @@ def test_noalloc_default_split_fits_the_static_array(cuda):
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
     import bench
     from astc_kv_cuda import _lib as L
-    wl = bench.Workload("c2", cuda, batch=1)
+    wl = bench.Workload("c2", cuda, batch=8)
     assert wl.attn.workspace.numel() * 4 > L.AKV_STATIC_WORKSPACE_BYTES
     ref = wl.attn.run().clone().cpu().numpy()
     for call in range(2):
