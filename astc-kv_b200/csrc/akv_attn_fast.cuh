@@ -20,13 +20,11 @@
 //   * Tensor cores (mma.sync m16n8k16, fp32 accumulation). Every warp owns
 //     one (16-token tile, half of the head dims) pair; the query heads of
 //     the GQA group are the N=8 dimension:
-//       S^T[tok][head] = K . Q^T   (q hi+lo; FP16 K either straight from
-//                                   global memory in fragment order,
-//                                   L2-prefetched a chunk ahead (6x6 V), or
-//                                   staged in shared memory by 16-byte
-//                                   cp.async copies issued a chunk ahead
-//                                   (4x4 / 8x8 V); or decoded K hi+lo; both
-//                                   warps of a tile compute it)
+//       S^T[tok][head] = K . Q^T   (q hi+lo; FP16 K staged in shared memory
+//                                   by 16-byte cp.async copies issued a
+//                                   chunk ahead (they land during the
+//                                   chunk's decode), or decoded K hi+lo;
+//                                   both warps of a tile compute it)
 //       online softmax per head in base 2, P^T as fp16 hi + lo through a
 //       512-byte per-warp buffer,
 //       O^T[dim][head] += V^T . P^T  for the warp's dim half (V hi and lo,
@@ -204,7 +202,7 @@ struct DecodeScratch {
     // Descriptor slots: every block of a small chunk (8x8 planes are mostly
     // reduced grids), at most 64; 40 for 6x6 planes (astcenc's 6x6 chunks
     // hold about ten descriptor blocks in 176).
-    static constexpr int kSlowMax = 64;
+    static constexpr int kSlowMax = BS == 6 ? 40 : 64;
     static constexpr int kSlowCap = NB < kSlowMax ? NB : kSlowMax;
     // Columns: one per decoding thread (a chunk with fewer blocks than
     // threads leaves the others idle).
@@ -682,12 +680,6 @@ struct Cfg {
     static constexpr int KMETA = KBS ? (KBLK > CH ? (KBLK > D ? KBLK : D) : (CH > D ? CH : D)) : 0;
     static constexpr int SIDE = KBS ? CH * 8 : 0;              // up to 8 side channels
     static constexpr int MAXBS = (VBS > KBS ? VBS : KBS);
-    // FP16 K with a 6x6 V plane: K fragments straight from global memory
-    // (L2-prefetched a chunk ahead), which leaves the shared memory to the
-    // decoder and L1 (measured on config 2: 4.65 ms against 4.77 with the K
-    // rows staged); other FP16-K instances stage the rows by cp.async
-    // (config 4's 4x4 V: 7.87 ms against 8.22).
-    static constexpr bool KDIRECT = KBS == 0 && VBS == 6;
     // CTAs per SM (shared memory allows three; scalar 4x4 V with FP16 K runs
     // two with more registers), and the register cap that fits them.
     static constexpr int CTAS = (VBS == 4 && KBS == 0 && VL == AKV_LAYOUT_SCALAR) ? 2 : 3;
@@ -716,7 +708,7 @@ struct Smem {
     __align__(16) __half kside[2][KBS ? C::SIDE : 1];
     __align__(16) __half vhi[C::CH][C::LD];
     __align__(16) __half vlo[C::CH][C::LD];
-    __align__(16) __half khi[(KBS || !C::KDIRECT) ? C::CH : 1][C::LD];  // decoded K hi, or staged FP16 K rows
+    __align__(16) __half khi[C::CH][C::LD];   // decoded K hi, or the staged FP16 K rows
     __align__(16) __half klo[KBS ? C::CH : 1][C::LD];
     __align__(16) uint8_t ds[C::DSBYTES];
     __align__(16) __half pbuf[2 * C::NWM][2][16][8];  // per warp: P hi, P lo as [token][head]
@@ -836,12 +828,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
         const int64_t qb = (static_cast<int64_t>(b) * p.Hq + h * G + (has ? qn : 0)) * D;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-            // Natural dim order for shared-memory K; a permuted order for
-            // direct FP16 K loads (lane quad j of a row loads dims
-            // [32 g + 8 j, 32 g + 8 j + 8) of each 32-dim group g).
-            int d0, d1;
-            if (!C::KDIRECT) { d0 = 16 * ks + 2 * qj; d1 = d0 + 8; }
-            else { const int g32 = ks >> 1, half = ks & 1; d0 = 32 * g32 + 8 * qj + 4 * half; d1 = d0 + 2; }
+            const int d0 = 16 * ks + 2 * qj, d1 = d0 + 8;
             const float q0 = has ? load_q(p.q, p.q_dtype, qb + d0) : 0.f;
             const float q1 = has ? load_q(p.q, p.q_dtype, qb + d0 + 1) : 0.f;
             const float q2 = has ? load_q(p.q, p.q_dtype, qb + d1) : 0.f;
@@ -856,7 +843,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
     // FP16 K rows of chunk c -> sm.khi by 16-byte asynchronous copies (rows
     // past the split or on unmapped pages copy zero bytes: zeros).
     auto stage_k = [&](int c) {
-        if constexpr (KBS == 0 && !C::KDIRECT) {
+        if constexpr (KBS == 0) {
             constexpr int PPR = D / 8, PIECES = CH * PPR;
             const int t0 = t_begin + c * CH;
             const uint8_t* kbase = p.k.data + b * p.k.sB + h * p.k.sH;
@@ -888,22 +875,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
             cp_async_commit();
         }
     };
-    // Direct K: L2 prefetch of chunk c's rows (one warp per token tile).
-    auto prefetch_k = [&](int c) {
-        if constexpr (C::KDIRECT) {
-            if (dh == 0 && c < nchunks) {
-                const int tt = t_begin + c * CH + 16 * tw + (lane >> 1);
-                if (tt < t_end && (lane & 1) * 128 < D * 2) {
-                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
-                    if (phys >= 0)
-                        prefetch_l2(p.k.data + b * p.k.sB + h * p.k.sH + static_cast<int64_t>(phys) * p.k.sP +
-                                    static_cast<int64_t>(tt % P) * D * 2 + (lane & 1) * 128);
-                }
-            }
-        }
-    };
     stage_k(0);
-    prefetch_k(0);
 
     float o[KH][4];
 #pragma unroll
@@ -923,7 +895,6 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
             break;
         }
         const bool valid = sm.valid[s] != 0;
-        prefetch_k(c + 1);
         // Decode V (and K) tiles.
         if constexpr (VL == AKV_LAYOUT_RGBA)
             decode_plane_rgba<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
@@ -974,31 +945,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
             }
             __syncthreads();
         }
-        if constexpr (KBS == 0 && !C::KDIRECT) {
+        if constexpr (KBS == 0) {
             // This chunk's K rows have landed (issued a chunk ahead).
             cp_async_wait<0>();
             __syncthreads();
-        }
-        // Direct FP16 K fragments for this warp's 16 tokens (loaded after the
-        // decode so they do not hold registers through it), permuted dims.
-        uint4 kreg[C::KDIRECT ? D / 32 : 1][2];
-        if constexpr (C::KDIRECT) {
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                const int tr = 16 * tw + qn + 8 * rr;
-                const int tt = t0 + tr;
-                const uint4* row = nullptr;
-                if (tr < n) {
-                    const int phys = phys_page(p.table, p.pps, p.num_pages, b, tt / P, nullptr);
-                    if (phys >= 0)
-                        row = reinterpret_cast<const uint4*>(p.k.data + b * p.k.sB + h * p.k.sH +
-                                                             static_cast<int64_t>(phys) * p.k.sP +
-                                                             static_cast<int64_t>(tt % P) * D * 2);
-                }
-#pragma unroll
-                for (int g32 = 0; g32 < D / 32; ++g32)
-                    kreg[g32][rr] = row ? __ldg(row + 4 * g32 + qj) : make_uint4(0u, 0u, 0u, 0u);
-            }
         }
         // The raw stage is consumed: refill it with chunk c + 2.
         if (tid == 0 && c + 2 < nchunks) {
@@ -1016,24 +966,15 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
                 const uint4 qf = sm.qfrag[ks][lane];
                 float* acc = sa[ks & 1];
                 uint32_t a[4];
-                if constexpr (C::KDIRECT) {
-                    const uint4 r0 = kreg[ks >> 1][0];
-                    const uint4 r1 = kreg[ks >> 1][1];
-                    if ((ks & 1) == 0) { a[0] = r0.x; a[2] = r0.y; a[1] = r1.x; a[3] = r1.y; }
-                    else { a[0] = r0.z; a[2] = r0.w; a[1] = r1.z; a[3] = r1.w; }
+                const int mi = lane >> 3, rr = lane & 7;
+                const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
+                const int col = 16 * ks + ((mi & 2) ? 8 : 0);
+                ldsm_x4(a, &sm.khi[row][col]);
+                mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
+                mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
+                if constexpr (KBS > 0) {
+                    ldsm_x4(a, &sm.klo[row][col]);
                     mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
-                } else {
-                    const int mi = lane >> 3, rr = lane & 7;
-                    const int row = 16 * tw + rr + ((mi & 1) ? 8 : 0);
-                    const int col = 16 * ks + ((mi & 2) ? 8 : 0);
-                    ldsm_x4(a, &sm.khi[row][col]);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                    mma16816(acc, a[0], a[1], a[2], a[3], qf.z, qf.w);
-                    if constexpr (KBS > 0) {
-                        ldsm_x4(a, &sm.klo[row][col]);
-                        mma16816(acc, a[0], a[1], a[2], a[3], qf.x, qf.y);
-                    }
                 }
             }
             float sacc[4];
@@ -1111,7 +1052,7 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
         __syncthreads();  // tiles and P buffers free for the next chunk
         if (c + 1 < nchunks) stage_k(c + 1);
     }
-    if constexpr (KBS == 0 && !C::KDIRECT) cp_async_wait<0>();  // nothing in flight past the loop
+    if constexpr (KBS == 0) cp_async_wait<0>();  // nothing in flight past the loop
 
     if (stuck) {
         // A copy never completed: report, give the copies still in flight
