@@ -374,18 +374,25 @@ __device__ __forceinline__ void write_block(const LumOut& o, const uint32_t* tab
 //   phase 1a thread per grid-weight row of the descriptor slots (when each
 //            thread decoded at most one block);
 //   phase 1b thread per texel row (6x6: texel pair) of the slotted blocks.
-template <int BS, int D, int THREADS, int NB, int LD>
+// RESET: clear the slot count here (one barrier); otherwise the caller
+// cleared it before its last barrier. wait_async: wait for the thread's
+// cp.async copies before the slot phase's first barrier, which then also
+// publishes them (the caller's next reads of those copies need no barrier
+// of their own).
+template <int BS, int D, int THREADS, int NB, int LD, bool RESET = true>
 __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* moff, const __half* mscl, int norm,
                                              int cols, int rows_blk, int n, bool valid,
                                              DecodeScratch<NB, THREADS, BS>& ds, __half (*thi)[LD],
-                                             __half (*tlo)[LD]) {
+                                             __half (*tlo)[LD], bool wait_async = false) {
     static_assert(BS % 2 == 0 && D % 8 == 0, "texel pairs; whole 8-texel rows");
     constexpr int kCap = DecodeScratch<NB, THREADS, BS>::kSlowCap;
     const int nblk = rows_blk * cols;
     const bool affine = norm == AKV_NORM_BLOCK_AFFINE;
     const int tid = threadIdx.x;
-    if (tid == 0) ds.nslot = 0;
-    __syncthreads();
+    if constexpr (RESET) {
+        if (tid == 0) ds.nslot = 0;
+        __syncthreads();
+    }
     // Work items: when the chunk's 4 x 8 tiles of blocks (block rows x block
     // columns) fit the scratch columns, lane l of item group g takes block
     // (4 tr + l / 8, 8 tc + l % 8) of tile g, so the lanes' pair stores into
@@ -455,6 +462,7 @@ __device__ __forceinline__ void decode_plane(const uint4* raw, const __half* mof
             }
         }
     }
+    if (wait_async) cp_async_wait<0>();
     __syncthreads();
     const int nslow = min(ds.nslot, kCap);
     if (nslow > 0) {
@@ -623,7 +631,7 @@ template <int D, int THREADS, int NB, int LD>
 __device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half* moff, const __half* mscl, int norm,
                                                   int cols, int rows_blk, int n, bool valid, int P,
                                                   DecodeScratch<NB, THREADS, 4>& ds, __half (*thi)[LD],
-                                                  __half (*tlo)[LD]) {
+                                                  __half (*tlo)[LD], bool wait_async = false) {
     constexpr int NC = DecodeScratch<NB, THREADS, 4>::NC;
     const int nblk = rows_blk * cols;
     const int tid = threadIdx.x;
@@ -653,6 +661,7 @@ __device__ __forceinline__ void decode_plane_rgba(const uint4* raw, const __half
         else
             write_rgba_n<LD, AKV_NORM_BLOCK_AFFINE>(o, codes, NC, i, bmoff, bmscl, row0, col0, rows, thi, tlo);
     }
+    if (wait_async) cp_async_wait<0>();
     __syncthreads();
 }
 
@@ -889,6 +898,10 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
         const int t0 = t_begin + c * CH;
         const int n = min(CH, t_end - t0);
         const bool waited = mbar_wait(&sm.bar[s], parity);
+        // The V plane's slot count restarts at zero; nothing reads it between
+        // the previous chunk's last barrier and the next one.
+        if constexpr (VL != AKV_LAYOUT_RGBA)
+            if (tid == 0) reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds)->nslot = 0;
         if (__syncthreads_or(!waited)) {
             stuck = true;
             if (tid == 0) sm.stuck_c = c;
@@ -900,12 +913,11 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
             decode_plane_rgba<D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS,
                                                       CH / 4, n, valid, P,
                                                       *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, 4>*>(sm.ds),
-                                                      sm.vhi, sm.vlo);
+                                                      sm.vhi, sm.vlo, KBS == 0);
         else
-            decode_plane<VBS, D, THREADS, C::VBLK, LD>(sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm,
-                                                      C::VCOLS, CH / VBS, n, valid,
-                                                      *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds),
-                                                      sm.vhi, sm.vlo);
+            decode_plane<VBS, D, THREADS, C::VBLK, LD, false>(
+                sm.vraw[s], sm.vmeta[s][0], sm.vmeta[s][1], p.v.norm, C::VCOLS, CH / VBS, n, valid,
+                *reinterpret_cast<DecodeScratch<C::VBLK, THREADS, VBS>*>(sm.ds), sm.vhi, sm.vlo, KBS == 0);
         if constexpr (KBS > 0) {
             constexpr int KB = KBS ? KBS : 4;
             constexpr int KN = KBS ? C::KBLK : 1;
@@ -945,11 +957,8 @@ __global__ void __launch_bounds__(Cfg<D, G, VBS, KBS, VL>::THREADS, Cfg<D, G, VB
             }
             __syncthreads();
         }
-        if constexpr (KBS == 0) {
-            // This chunk's K rows have landed (issued a chunk ahead).
-            cp_async_wait<0>();
-            __syncthreads();
-        }
+        // FP16 K: this chunk's rows (issued a chunk ahead) were waited for
+        // inside the V decode, before a barrier.
         // The raw stage is consumed: refill it with chunk c + 2.
         if (tid == 0 && c + 2 < nchunks) {
             fence_proxy_async();
