@@ -73,65 +73,21 @@ __device__ __forceinline__ void mask_u128(uint64_t& lo, uint64_t& hi, int n) {
     if (n < 128) hi &= (1ull << (n - 64)) - 1ull;
 }
 
-// Decode one BISE value group. `win` holds the group's bits at bit 0.
-// Returns the digits of the trit/quint block packed (2 bits per trit, 3 per quint).
-__device__ __forceinline__ uint32_t group_digits(uint64_t win, int b, int trits, int quints) {
-    const Tables& T = g_akv_tables;
-    if (trits) {
-        uint32_t t = static_cast<uint32_t>((win >> b) & 3u) |
-                     static_cast<uint32_t>(((win >> (2 * b + 2)) & 3u) << 2) |
-                     static_cast<uint32_t>(((win >> (3 * b + 4)) & 1u) << 4) |
-                     static_cast<uint32_t>(((win >> (4 * b + 5)) & 3u) << 5) |
-                     static_cast<uint32_t>(((win >> (5 * b + 7)) & 1u) << 7);
-        return __ldg(&T.trit[t]);
-    }
-    if (quints) {
-        uint32_t qv = static_cast<uint32_t>((win >> b) & 7u) |
-                      static_cast<uint32_t>(((win >> (2 * b + 3)) & 3u) << 3) |
-                      static_cast<uint32_t>(((win >> (3 * b + 5)) & 3u) << 5);
-        return __ldg(&T.quint[qv]);
-    }
-    return 0;
-}
-
-// BISE decode of `count` values of range q from the 128-bit stream (lo, hi)
-// that starts at bit 0 and is already masked to its own length.
-// `sink(i, code)` receives each raw code.
-template <typename Sink>
-__device__ __forceinline__ void bise_stream(uint64_t lo, uint64_t hi, int count, int q, Sink&& sink) {
-    const uint32_t shp = __ldg(&g_akv_tables.shape[q]);
-    const int b = shp & 15, trits = (shp >> 4) & 1, quints = (shp >> 5) & 1;
-    const int gs = quints ? 3 : 5;
-    const int gbits = trits ? 5 * b + 8 : (quints ? 3 * b + 7 : 5 * b);
-    const uint32_t mmask = (1u << b) - 1u;
-    int base = 0;
-    for (int i = 0; i < count; i += gs, base += gbits) {
-        const uint64_t win = window_u128(lo, hi, base);
-        const uint32_t dg = group_digits(win, b, trits, quints);
-#pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            if (j >= gs || i + j >= count) break;
-            // Offset of the j-th value's low bits within the group.
-            const int off = j * b + (trits ? (j == 0 ? 0 : j == 1 ? 2 : j == 2 ? 4 : j == 3 ? 5 : 7)
-                                           : (quints ? (j == 0 ? 0 : j == 1 ? 3 : 5) : 0));
-            const uint32_t m = static_cast<uint32_t>(win >> off) & mmask;
-            const uint32_t d = trits ? ((dg >> (2 * j)) & 3u) : (quints ? ((dg >> (3 * j)) & 7u) : 0u);
-            sink(i + j, static_cast<int>((d << b) | m));
-        }
-    }
-}
-
 // BISE weight codes: `count` values of range wq from the bit-reversed weight
-// stream (s0, s1), already masked to its length, into codes[i * nt]. Groups
-// of five (trits, plain bits) or three (quints) values per step, with the
-// trit/quint block bits gathered by runtime shifts and decoded through the
-// combined digit table. Every step stores five codes without predicates: a
-// quint step's two extra codes are overwritten by the next step, and the
-// last step may write up to four rows past `count` (the caller provides
-// kCodePad rows of slack).
+// stream (s0, s1), already masked to its length, into codes[i * nt] (UNQ:
+// the unquantised weights un[code] instead). Groups of five (trits, plain
+// bits) or three (quints) values per step, with the trit/quint block bits
+// gathered by runtime shifts and decoded through the combined digit table.
+// Every step stores five codes without predicates: a quint step's two extra
+// codes are overwritten by the next step, and the last step may write up to
+// four rows past `count` (the caller provides kCodePad rows of slack). Every
+// code a step forms, the extra ones included, lies inside its range's row of
+// the unquantisation table.
 constexpr int kCodePad = 4;
 
-__device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, int count, uint8_t* codes, int nt) {
+template <bool UNQ = false>
+__device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, int count, uint8_t* codes, int nt,
+                                             const uint8_t* un = nullptr) {
     const Tables& T = g_akv_tables;
     const uint32_t shp = __ldg(&T.shape[wq]);
     const int b = shp & 15;
@@ -163,11 +119,24 @@ __device__ __forceinline__ void weight_codes(uint64_t s0, uint64_t s1, int wq, i
         const uint32_t X = ((win >> b) & m1) | ((win >> b2) & m2) | ((win >> b3) & m3) | ((win >> b4) & m4) |
                            ((win >> b5) & m5);
         const uint32_t dgb = static_cast<uint32_t>(__ldg(dig + X)) << b;
-        cp[0] = static_cast<uint8_t>((dgb & km) | (win & bm));
-        cp[nt] = static_cast<uint8_t>(((dgb >> 3) & km) | ((win >> o1) & bm));
-        cp[2 * nt] = static_cast<uint8_t>(((dgb >> 6) & km) | ((win >> o2) & bm));
-        cp[3 * nt] = static_cast<uint8_t>(((dgb >> 9) & km) | ((win >> o3) & bm));
-        cp[4 * nt] = static_cast<uint8_t>(((dgb >> 12) & km) | ((win >> o4) & bm));
+        const uint32_t c0 = (dgb & km) | (win & bm);
+        const uint32_t c1 = ((dgb >> 3) & km) | ((win >> o1) & bm);
+        const uint32_t c2 = ((dgb >> 6) & km) | ((win >> o2) & bm);
+        const uint32_t c3 = ((dgb >> 9) & km) | ((win >> o3) & bm);
+        const uint32_t c4 = ((dgb >> 12) & km) | ((win >> o4) & bm);
+        if constexpr (UNQ) {
+            cp[0] = __ldg(un + c0);
+            cp[nt] = __ldg(un + c1);
+            cp[2 * nt] = __ldg(un + c2);
+            cp[3 * nt] = __ldg(un + c3);
+            cp[4 * nt] = __ldg(un + c4);
+        } else {
+            cp[0] = static_cast<uint8_t>(c0);
+            cp[nt] = static_cast<uint8_t>(c1);
+            cp[2 * nt] = static_cast<uint8_t>(c2);
+            cp[3 * nt] = static_cast<uint8_t>(c3);
+            cp[4 * nt] = static_cast<uint8_t>(c4);
+        }
         cp += step;
         w0 = __funnelshift_r(w0, w1, gb);
         w1 = __funnelshift_r(w1, w2, gb);
@@ -183,6 +152,49 @@ __device__ __forceinline__ int bise_stream_bits_dev(int count, int q) {
     return count * b + (((shp >> 4) & 1) ? (8 * count + 4) / 5 : 0) + (((shp >> 5) & 1) ? (7 * count + 2) / 3 : 0);
 }
 
+// The first nv colour integers of range cq from the colour stream (s0, s1),
+// masked to its length, unquantised to 0..255 into out[j * nt]: one runtime
+// step loop for trit, quint and plain-bit ranges alike (64-bit windows:
+// colour groups reach 40 bits). Writes up to four values past nv (callers
+// have the slack).
+__device__ __forceinline__ void color_values(uint64_t s0, uint64_t s1, int cq, int nv, uint8_t* out, int nt) {
+    const Tables& T = g_akv_tables;
+    const uint32_t shp = __ldg(&T.shape[cq]);
+    const int b = shp & 15;
+    const bool tr = (shp >> 4) & 1, qu = (shp >> 5) & 1;
+    const int gs = qu ? 3 : 5;
+    const int gb = tr ? 5 * b + 8 : (qu ? 3 * b + 7 : 5 * b);
+    const int ng = qu ? (nv + 2) / 3 : (nv + 4) / 5;
+    const uint64_t m1 = tr ? 0x03u : (qu ? 0x07u : 0u);
+    const uint64_t m2 = tr ? 0x0Cu : (qu ? 0x18u : 0u);
+    const uint64_t m3 = tr ? 0x10u : (qu ? 0x60u : 0u);
+    const uint64_t m4 = tr ? 0x60u : 0u;
+    const uint64_t m5 = tr ? 0x80u : 0u;
+    const int o1 = b + (tr ? 2 : (qu ? 3 : 0));
+    const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
+    const int o3 = 3 * b + (tr ? 5 : 0);
+    const int o4 = 4 * b + (tr ? 7 : 0);
+    const uint16_t* dig = T.dig3 + (qu ? 256 : 0);
+    const uint8_t* un = T.cunq[cq];
+    const uint64_t bm = (1ull << b) - 1ull;
+    uint8_t* cp = out;
+    for (int g = 0; g < ng; ++g) {
+        const uint64_t win = s0;
+        const uint32_t X = static_cast<uint32_t>(((win >> b) & m1) | ((win >> (2 * b)) & m2) |
+                                                 ((win >> (3 * b)) & m3) | ((win >> (4 * b)) & m4) |
+                                                 ((win >> (5 * b)) & m5));
+        const uint32_t dg = __ldg(dig + X);
+        cp[0] = __ldg(un + (((dg & 7u) << b) | static_cast<uint32_t>(win & bm)));
+        cp[nt] = __ldg(un + ((((dg >> 3) & 7u) << b) | static_cast<uint32_t>((win >> o1) & bm)));
+        cp[2 * nt] = __ldg(un + ((((dg >> 6) & 7u) << b) | static_cast<uint32_t>((win >> o2) & bm)));
+        cp[3 * nt] = __ldg(un + ((((dg >> 9) & 7u) << b) | static_cast<uint32_t>((win >> o3) & bm)));
+        cp[4 * nt] = __ldg(un + ((((dg >> 12) & 7u) << b) | static_cast<uint32_t>((win >> o4) & bm)));
+        cp += gs * nt;
+        s0 = (s0 >> gb) | (s1 << (64 - gb));
+        s1 >>= gb;
+    }
+}
+
 __device__ __forceinline__ int clamp8(int v) { return v < 0 ? 0 : (v > 255 ? 255 : v); }
 
 // Signed bit transfer between a (offset) and b (base), spec form.
@@ -192,9 +204,9 @@ __device__ __forceinline__ void bit_xfer(int& a, int& b) {
     if (a & 0x20) a -= 0x40;
 }
 
-// LDR endpoint modes -> 8-bit endpoint pair per channel. Returns false for HDR
-// modes (2, 3, 7, 11, 14, 15).
-__device__ __forceinline__ bool endpoints(int cem, const int* v, int e0[4], int e1[4]) {
+// LDR endpoint modes -> 8-bit endpoint pair per channel, from the mode's
+// colour integers v[0..]. Returns false for HDR modes (2, 3, 7, 11, 14, 15).
+__device__ __forceinline__ bool endpoints(int cem, const uint8_t* v, int (&e0)[4], int (&e1)[4]) {
     switch (cem) {
         case 0:
             e0[0] = e0[1] = e0[2] = v[0]; e1[0] = e1[1] = e1[2] = v[1]; e0[3] = e1[3] = 255;
@@ -218,6 +230,7 @@ __device__ __forceinline__ bool endpoints(int cem, const int* v, int e0[4], int 
         }
         case 6:
         case 10:
+#pragma unroll
             for (int c = 0; c < 3; ++c) { e0[c] = (v[c] * v[3]) >> 8; e1[c] = v[c]; }
             e0[3] = cem == 10 ? v[4] : 255;
             e1[3] = cem == 10 ? v[5] : 255;
@@ -237,17 +250,21 @@ __device__ __forceinline__ bool endpoints(int cem, const int* v, int e0[4], int 
         case 9:
         case 13: {
             int o[4], bse[4];
+#pragma unroll
             for (int c = 0; c < 3; ++c) { o[c] = v[2 * c + 1]; bse[c] = v[2 * c]; bit_xfer(o[c], bse[c]); }
             if (cem == 13) { o[3] = v[7]; bse[3] = v[6]; bit_xfer(o[3], bse[3]); }
             else { o[3] = 0; bse[3] = 255; }
             int lo[4], hi[4];
+#pragma unroll
             for (int c = 0; c < 4; ++c) { lo[c] = bse[c]; hi[c] = bse[c] + o[c]; }
             if (o[0] + o[1] + o[2] < 0) {  // blue contraction, endpoints swapped
                 int t[4];
+#pragma unroll
                 for (int c = 0; c < 4; ++c) { t[c] = hi[c]; hi[c] = lo[c]; lo[c] = t[c]; }
                 lo[0] = (lo[0] + lo[2]) >> 1; lo[1] = (lo[1] + lo[2]) >> 1;
                 hi[0] = (hi[0] + hi[2]) >> 1; hi[1] = (hi[1] + hi[2]) >> 1;
             }
+#pragma unroll
             for (int c = 0; c < 4; ++c) { e0[c] = clamp8(lo[c]); e1[c] = clamp8(hi[c]); }
             return true;
         }
@@ -297,60 +314,74 @@ __device__ __forceinline__ void decode_header(uint4 blk, int fp, BlockDesc<NCH>&
     if (dual && parts == 4) { set_error(); return; }
 
     const int top = 128 - wbits - 2 * dual;  // first bit above the colour data
-    int cem[4];
+    // Endpoint modes of partitions 0..3, four bits each (no array: the
+    // partition loop below indexes them at run time).
+    uint32_t cems;
     int cstart, extra = 0, seed = 0;
     if (parts == 1) {
-        cem[0] = static_cast<int>((lo >> 13) & 15);
+        cems = static_cast<uint32_t>((lo >> 13) & 15);
         cstart = 17;
     } else {
         seed = static_cast<int>((lo >> 13) & 0x3FF);
         const int field = static_cast<int>((lo >> 23) & 0x3F);
         cstart = 29;
         if ((field & 3) == 0) {
-            for (int p = 0; p < 4; ++p) cem[p] = field >> 2;
+            cems = static_cast<uint32_t>(field >> 2) * 0x1111u;
         } else {
             extra = 3 * parts - 4;
             const int all = (field >> 2) | (static_cast<int>(bits_u128(lo, hi, top - extra, extra)) << 4);
             const int cls = (field & 3) - 1;
+            cems = 0u;
+#pragma unroll
             for (int p = 0; p < 4; ++p)
-                cem[p] = ((cls + ((all >> p) & 1)) << 2) | ((all >> (parts + 2 * p)) & 3);
+                cems |= static_cast<uint32_t>(((cls + ((all >> p) & 1)) << 2) | ((all >> (parts + 2 * p)) & 3))
+                        << (4 * p);
         }
     }
     int npairs = 0;
-    for (int p = 0; p < parts; ++p) npairs += (cem[p] >> 2) + 1;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+        if (p < parts) npairs += static_cast<int>((cems >> (4 * p + 2)) & 3u) + 1;
     const int avail = top - extra - cstart;
     if (npairs > 9 || avail < 0) { set_error(); return; }
     const int cq = T.cquant[npairs][avail];
     if (cq == 0xFF) { set_error(); return; }
 
-    // Colour integers.
-    int vals[18];
+    // Colour integers, unquantised, into w[0 .. 2 npairs) (at most 18 values
+    // plus 4 of slack; the weights overwrite them below).
     {
         uint64_t clo = window_u128(lo, hi, cstart);
-        uint64_t chi = cstart == 0 ? hi : (hi >> cstart);
-        const int cbits = bise_stream_bits_dev(2 * npairs, cq);
-        mask_u128(clo, chi, cbits);
-        bise_stream(clo, chi, 2 * npairs, cq, [&](int i, int code) { vals[i] = __ldg(&T.cunq[cq][code]); });
+        uint64_t chi = hi >> cstart;
+        mask_u128(clo, chi, bise_stream_bits_dev(2 * npairs, cq));
+        color_values(clo, chi, cq, 2 * npairs, w, 1);
     }
-    int e0[4][4], e1[4][4];
+    // Endpoints: each partition's pair per channel, packed as the bytes of
+    // e0p[c] / e1p[c] (byte p = partition p).
+    uint32_t e0p[NCH], e1p[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) e0p[c] = e1p[c] = 0u;
     {
         int k = 0;
         for (int p = 0; p < parts; ++p) {
-            if (!endpoints(cem[p], vals + k, e0[p], e1[p])) { set_error(); return; }
-            k += 2 * ((cem[p] >> 2) + 1);
+            const int cem = static_cast<int>((cems >> (4 * p)) & 15u);
+            int e0[4], e1[4];
+            if (!endpoints(cem, w + k, e0, e1)) { set_error(); return; }
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                e0p[c] |= static_cast<uint32_t>(e0[c]) << (8 * p);
+                e1p[c] |= static_cast<uint32_t>(e1[c]) << (8 * p);
+            }
+            k += 2 * ((cem >> 2) + 1);
         }
     }
 
     // Weights: the stream runs downward from bit 127; bit-reverse the block.
+    // Unquantised five per step (writes up to kCodePad bytes past n).
     {
         uint64_t wlo = __brevll(hi), whi = __brevll(lo);
         mask_u128(wlo, whi, wbits);
         const int n = wx * wy * (dual + 1);
-        // Raw codes five per step (writes up to kCodePad bytes past n), then
-        // unquantised in place.
-        weight_codes(wlo, whi, wq, n, w, 1);
-        const uint8_t* un = T.wunq[wq];
-        for (int i = 0; i < n; ++i) w[i] = __ldg(un + w[i]);
+        weight_codes<true>(wlo, whi, wq, n, w, 1, T.wunq[wq]);
     }
 
     const int ccs = dual ? static_cast<int>(bits_u128(lo, hi, 128 - wbits - 2, 2)) : 0;
@@ -367,7 +398,8 @@ __device__ __forceinline__ void decode_header(uint4 blk, int fp, BlockDesc<NCH>&
     for (int p = 0; p < 4; ++p)
 #pragma unroll
         for (int c = 0; c < NCH; ++c)
-            d.ep[p * NCH + c] = (p < parts) ? static_cast<uint32_t>(e0[p][c] | (e1[p][c] << 8)) : 0u;
+            d.ep[p * NCH + c] = (p < parts) ? (((e0p[c] >> (8 * p)) & 0xFFu) | (((e1p[c] >> (8 * p)) & 0xFFu) << 8))
+                                            : 0u;
 }
 
 

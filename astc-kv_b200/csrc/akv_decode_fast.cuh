@@ -97,49 +97,6 @@ __device__ __forceinline__ int block_kind(uint4 blk, uint32_t& me, int& cq) {
     return kKindTable;
 }
 
-// The first nv (<= 8) colour integers of range cq from the colour stream
-// (s0, s1), masked to its length, unquantised to 0..255 into out[j * nt]:
-// one runtime step loop for trit, quint and plain-bit ranges alike (64-bit
-// windows: colour groups reach 40 bits). Writes up to four values past nv
-// (callers have the slack).
-__device__ __forceinline__ void color_values(uint64_t s0, uint64_t s1, int cq, int nv, uint8_t* out, int nt) {
-    const Tables& T = g_akv_tables;
-    const uint32_t shp = __ldg(&T.shape[cq]);
-    const int b = shp & 15;
-    const bool tr = (shp >> 4) & 1, qu = (shp >> 5) & 1;
-    const int gs = qu ? 3 : 5;
-    const int gb = tr ? 5 * b + 8 : (qu ? 3 * b + 7 : 5 * b);
-    const int ng = qu ? (nv + 2) / 3 : (nv + 4) / 5;
-    const uint64_t m1 = tr ? 0x03u : (qu ? 0x07u : 0u);
-    const uint64_t m2 = tr ? 0x0Cu : (qu ? 0x18u : 0u);
-    const uint64_t m3 = tr ? 0x10u : (qu ? 0x60u : 0u);
-    const uint64_t m4 = tr ? 0x60u : 0u;
-    const uint64_t m5 = tr ? 0x80u : 0u;
-    const int o1 = b + (tr ? 2 : (qu ? 3 : 0));
-    const int o2 = 2 * b + (tr ? 4 : (qu ? 5 : 0));
-    const int o3 = 3 * b + (tr ? 5 : 0);
-    const int o4 = 4 * b + (tr ? 7 : 0);
-    const uint16_t* dig = T.dig3 + (qu ? 256 : 0);
-    const uint8_t* un = T.cunq[cq];
-    const uint64_t bm = (1ull << b) - 1ull;
-    uint8_t* cp = out;
-    for (int g = 0; g < ng; ++g) {
-        const uint64_t win = s0;
-        const uint32_t X = static_cast<uint32_t>(((win >> b) & m1) | ((win >> (2 * b)) & m2) |
-                                                 ((win >> (3 * b)) & m3) | ((win >> (4 * b)) & m4) |
-                                                 ((win >> (5 * b)) & m5));
-        const uint32_t dg = __ldg(dig + X);
-        cp[0] = __ldg(un + (((dg & 7u) << b) | static_cast<uint32_t>(win & bm)));
-        cp[nt] = __ldg(un + ((((dg >> 3) & 7u) << b) | static_cast<uint32_t>((win >> o1) & bm)));
-        cp[2 * nt] = __ldg(un + ((((dg >> 6) & 7u) << b) | static_cast<uint32_t>((win >> o2) & bm)));
-        cp[3 * nt] = __ldg(un + ((((dg >> 9) & 7u) << b) | static_cast<uint32_t>((win >> o3) & bm)));
-        cp[4 * nt] = __ldg(un + ((((dg >> 12) & 7u) << b) | static_cast<uint32_t>((win >> o4) & bm)));
-        cp += gs * nt;
-        s0 = (s0 >> gb) | (s1 << (64 - gb));
-        s1 >>= gb;
-    }
-}
-
 // Value table of a luminance-direct block: entry q * L + code at
 // tab[entry * nt], two entries per step (fp16 hi/lo packing on pairs).
 __device__ __forceinline__ void build_table(const int (&v)[8], int parts, int wq, int L, bool affine, float sc,

@@ -14,11 +14,12 @@ constexpr int kDecodeBlocksPerIter = 256;  // one header per thread: no warp idl
 // consecutive threads on consecutive rows so the output stays contiguous
 // across a warp: with VEC (out 16-byte aligned) each row leaves in 16-byte
 // (8-byte for 6x6 UNORM8) vector stores, else in 32-bit words.
-// Three CTAs per SM (registers capped at 80; the 8x8 instance would take
-// 83 and drop to two); weight rows padded to 68 bytes so the row tasks of
-// different blocks in a warp read different banks.
+// Four CTAs per SM (registers capped at 64, no spills: the header decoder
+// keeps its colour integers in the block's weight row and its endpoints in
+// packed registers, so it needs no local memory); weight rows padded to 68
+// bytes so the row tasks of different blocks in a warp read different banks.
 template <int BS, int MODE, bool VEC>
-__global__ void __launch_bounds__(kDecodeThreads, 3) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
+__global__ void __launch_bounds__(kDecodeThreads, 4) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
                                                                           void* __restrict__ out) {
     __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
     __shared__ uint8_t wts[kDecodeBlocksPerIter][64 + kCodePad];
