@@ -97,9 +97,16 @@ def peaks() -> tuple[float, str]:
 def profile_traffic(workload: str) -> tuple[float | None, str | None]:
     """Per-launch DRAM traffic of the split kernel for a full launch, read from
     the workload's committed ncu summary (profiles/*_<workload>.md, line
-    ``traffic_bytes_per_full_launch: N``). None when no summary carries it."""
+    ``traffic_bytes_per_full_launch: N``; or any summary covering several
+    workloads, line ``traffic_bytes_per_full_launch[<workload>]: N``). None
+    when no summary carries it."""
     for f in sorted((ROOT / "profiles").glob(f"*_{workload}.md")):
         m = re.search(r"^traffic_bytes_per_full_launch:\s*([0-9.eE+]+)", f.read_text(), re.M)
+        if m:
+            return float(m.group(1)), f.name
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        m = re.search(r"^traffic_bytes_per_full_launch\[" + re.escape(workload) + r"\]:\s*([0-9.eE+]+)",
+                      f.read_text(), re.M)
         if m:
             return float(m.group(1)), f.name
     return None, None
@@ -704,6 +711,10 @@ def run_ours(args) -> dict | None:
     achieved = wl.bytes / (split_ms * 1e-3) / 1e9
     toks = job_units * args.steps
     traffic, traffic_src = profile_traffic(args.workload)
+    if traffic is not None:
+        # The committed figure is for the whole job on one GPU; a rank's shard
+        # (or a smaller profiling case) moves its share of it.
+        traffic = traffic * wl.bytes / job_bytes(args.workload)
     cfg = line_config(args.workload, world, shard)
     if args.batch:
         cfg["batch_override"] = args.batch
@@ -923,6 +934,10 @@ def run_decode(args) -> dict | None:
     hbm, src = peaks()
     per = total_ms / args.steps
     achieved = wl.bytes / (per * 1e-3) / 1e9
+    # The committed figure is for a launch of the default 2^26 blocks.
+    traffic, traffic_src = profile_traffic(args.workload)
+    if traffic is not None:
+        traffic = traffic * wl.n / float(1 << 26)
     line = {"metric": METRIC + " [decode microbench: blocks/s]", "value": wl.n * world * args.steps / (total_ms * 1e-3),
             "unit": "blocks/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": per,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
@@ -930,7 +945,8 @@ def run_decode(args) -> dict | None:
             "config": {**wl.desc, "parallelism": f"replicas x{world}, no collective"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                          "peak_source": src, "kernel": "decode_blocks_kernel", "kernel_ms": per,
-                         "traffic": None, "bytes": "16 B read + texels*4 B written per block"},
+                         "traffic": traffic, "traffic_source": traffic_src and f"profiles/{traffic_src}",
+                         "bytes": "16 B read + texels*4 B written per block"},
             "e2e": {"value": n_e2e * world * args.steps / (e2e_ms * 1e-3), "unit": "blocks/s",
                     "h2d_bytes_per_step": n_e2e * 16, "d2h_bytes_per_step": n_e2e * wl.block * wl.block * 4,
                     "api": "astc_kv_cuda.ops.decode_blocks (akv_cuda_decode_blocks)",
