@@ -18,17 +18,64 @@ constexpr int kDecodeBlocksPerIter = 256;  // one header per thread: no warp idl
 // keeps its colour integers in the block's weight row and its endpoints in
 // packed registers, so it needs no local memory); weight rows padded to 68
 // bytes so the row tasks of different blocks in a warp read different banks.
+// Before stage A the iteration's blocks are ordered by header class
+// (partition count, endpoint-mode class, void extent: header_class), so a
+// warp's lanes mostly decode blocks that take the same branches; each block
+// still lands in its own descriptor slot, so the output does not depend on
+// the order.
+constexpr int kHeaderClasses = 17;
+static_assert(kHeaderClasses <= 32, "one warp scans the class counts");
+
+__device__ __forceinline__ int header_class(uint4 blk) {
+    const uint32_t x = blk.x;
+    if ((x & 0x1FF) == 0x1FC) return 16;  // void extent
+    const int parts = static_cast<int>((x >> 11) & 3);  // partition count - 1
+    int cls;                                            // endpoint mode >> 2 (of partition 0's class)
+    if (parts == 0) {
+        cls = static_cast<int>((x >> 15) & 3);
+    } else {
+        const int field = static_cast<int>((x >> 23) & 63);
+        cls = (field & 3) ? (field & 3) - 1 : field >> 4;
+    }
+    return (parts << 2) | cls;
+}
+
 template <int BS, int MODE, bool VEC>
 __global__ void __launch_bounds__(kDecodeThreads, 4) decode_blocks_kernel(const uint4* __restrict__ blocks, int64_t n,
                                                                           void* __restrict__ out) {
     __shared__ BlockDesc<4> desc[kDecodeBlocksPerIter];
     __shared__ uint8_t wts[kDecodeBlocksPerIter][64 + kCodePad];
+    __shared__ int cls_start[32];
+    __shared__ uint8_t order[kDecodeBlocksPerIter];
     constexpr int fp = footprint_index(BS);
     constexpr int TPB = BS * BS;
+    const int tid = threadIdx.x;
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * kDecodeBlocksPerIter; base < n;
          base += static_cast<int64_t>(gridDim.x) * kDecodeBlocksPerIter) {
         const int nb = static_cast<int>(min(static_cast<int64_t>(kDecodeBlocksPerIter), n - base));
-        if (threadIdx.x < nb) decode_header<4>(__ldg(blocks + base + threadIdx.x), fp, desc[threadIdx.x], wts[threadIdx.x]);
+        // Counting sort of the iteration's blocks by header class.
+        const int key = tid < nb ? header_class(__ldg(blocks + base + tid)) : 0;
+        if (tid < 32) cls_start[tid] = 0;
+        __syncthreads();
+        const int rank = tid < nb ? atomicAdd(&cls_start[key], 1) : 0;
+        __syncthreads();
+        if (tid < 32) {
+            const int c = cls_start[tid];
+            int incl = c;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int o = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+                if (tid >= d) incl += o;
+            }
+            cls_start[tid] = incl - c;
+        }
+        __syncthreads();
+        if (tid < nb) order[cls_start[key] + rank] = static_cast<uint8_t>(tid);
+        __syncthreads();
+        if (tid < nb) {
+            const int i = order[tid];
+            decode_header<4>(__ldg(blocks + base + i), fp, desc[i], wts[i]);
+        }
         __syncthreads();
         constexpr int WPT = MODE == AKV_OUT_UNORM8 ? 1 : 2;  // 32-bit output words per texel
         constexpr int NW = BS * WPT;                             // words per texel row
