@@ -48,6 +48,24 @@ def test_random_legal_blocks(cuda, bs, mode, omode, dt):
 
 
 @pytest.mark.parametrize("bs", [4, 6, 8])
+def test_block_order_does_not_change_any_block(cuda, bs):
+    # The kernel reorders each group of 256 blocks by header class before the
+    # header stage. A block's texels must not depend on its neighbours: a
+    # permutation of the input permutes the output, for a random order, for
+    # an input already grouped into long runs of one partition count, and
+    # with a ragged last group.
+    from astc_kv_cuda.ops import random_blocks
+    blocks = random_blocks(4 * 256 + 77, bs, seed=11 * bs)
+    base = gpu_decode(blocks, bs, "unorm16")
+    np.testing.assert_array_equal(base, O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
+    perm = np.random.default_rng(5).permutation(len(blocks))
+    np.testing.assert_array_equal(gpu_decode(blocks[perm], bs, "unorm16"), base[perm])
+    parts = (blocks[:, 1] >> 3) & 3  # header bits 11-12: partition count - 1
+    grouped = np.argsort(parts, kind="stable")
+    np.testing.assert_array_equal(gpu_decode(blocks[grouped], bs, "unorm16"), base[grouped])
+
+
+@pytest.mark.parametrize("bs", [4, 6, 8])
 def test_random_bytes_error_colour(cuda, bs):
     blocks = np.random.default_rng(99 + bs).integers(0, 256, (30011, 16), dtype=np.uint8)
     np.testing.assert_array_equal(gpu_decode(blocks, bs, "unorm16"), O.decode_blocks(blocks, bs, O.OUT_UNORM16, threads=4))
